@@ -1,0 +1,379 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 token sampler (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N=1 runs configuration 3 (batch 256 x vocab 151,936 bf16, all penalties, top-k 20, top-p 0.8,
+temperature 0.7): the north-star workload. N>1 (one process per GPU under torchrun, NCCL) runs
+configuration 4 vocab-sharded: batch 1,024 x vocab 248,320 bf16 split evenly over the ranks,
+local top-k 50 records, one all-gather, a merge on every rank. A step is one pass of the
+sampler over one batch. Inputs are seeded synthetic logits resident in HBM; four rotating
+logits buffers (more than 2x the 126 MB L2 in total) make every step read from HBM.
+
+``value`` is rows/s for the whole job (device time, max over ranks). ``e2e`` is the same
+metric through the public API with host (pinned) inputs copied in and the ids copied out in
+every step. ``roofline`` relates the sampler kernel's algorithmic bytes to its CUDA-event
+duration and the measured HBM copy bandwidth. ``cpu_baseline`` times vinfer's own sampler
+restated in PyTorch (``oracle/reference_port.py``) on this host's cores over a bounded sample.
+``--impl reference`` times only that CPU sampler, with the same metric and config.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+L2_BYTES = 126 * 1024 * 1024
+SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+# ----------------------------------------------------------------------------------------------
+# helpers
+# ----------------------------------------------------------------------------------------------
+def dist_env() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons around the timed region."""
+
+    def __init__(self, gpu: int) -> None:
+        self.gpu = gpu
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="clocks", suffix=".csv")[1])
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={SMI_FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), float(f[3]), f[4:]))
+            except ValueError:
+                continue
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[3][1:]) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
+
+
+def measured_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(workload: str) -> float | None:
+    """DRAM bytes per launch of the sampler kernel, from the committed ncu summary."""
+    p = ROOT / "profiles" / "roofline_traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == workload:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_reference_rows_per_s(w, seconds: float, rows_cap: int | None = None) -> dict:
+    """vinfer's sampler (restated in torch, with the build's penalty/min-p extensions) on this
+    host, one row per call as the runtime calls it; time-bounded sample of the workload."""
+    sys.path.insert(0, str(ROOT))
+    from oracle.reference_port import extended_sample  # noqa: PLC0415
+    from oracle.sampler_oracle import RowParams as OracleParams  # noqa: PLC0415
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    done = 0
+    t0 = time.perf_counter()
+    r = 0
+    while True:
+        p = OracleParams(temperature=float(w.temperature[r]), top_k=int(w.top_k[r]),
+                         top_p=float(w.top_p[r]), min_p=float(w.min_p[r]),
+                         repetition_penalty=float(w.repetition_penalty[r]),
+                         presence_penalty=float(w.presence_penalty[r]),
+                         frequency_penalty=float(w.frequency_penalty[r]))
+        ids = cnt = None
+        if w.hist_row_ptr is not None:
+            a, b = int(w.hist_row_ptr[r]), int(w.hist_row_ptr[r + 1])
+            ids, cnt = w.hist_ids[a:b], w.hist_counts[a:b]
+        extended_sample(w.logits[r], p, seed=r, position=done, hist_ids=ids, hist_counts=cnt)
+        done += 1
+        r = (r + 1) % w.batch
+        el = time.perf_counter() - t0
+        if (rows_cap is not None and done >= rows_cap) or (rows_cap is None and el >= seconds):
+            break
+    el = time.perf_counter() - t0
+    return {"value": done / el, "unit": "rows/s", "cores": threads, "kind": "port",
+            "sample": f"{done} rows of {w.name} (one sample() call per row) in {el:.1f} s"}
+
+
+# ----------------------------------------------------------------------------------------------
+# single GPU: configuration 3
+# ----------------------------------------------------------------------------------------------
+def bench_single(args) -> dict:
+    from vinfer_b200 import SAMPLER, BackendContext  # noqa: PLC0415
+    from vinfer_b200.sampling import RowParams, TokenHistogram  # noqa: PLC0415
+    from vinfer_b200.workloads import make  # noqa: PLC0415
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    w = make(3)
+    B, V = w.batch, w.vocab
+    backend = SAMPLER.resolve("b200", BackendContext(dev, torch.bfloat16))
+    nbuf = max(4, int(np.ceil(2 * L2_BYTES / (w.logits.numel() * 2))) + 1)
+    base = w.logits.to(dev)
+    bufs = [base] + [base.clone() for _ in range(nbuf - 1)]
+    params = RowParams.from_arrays(dev, **w.param_arrays())
+    u = torch.from_numpy(w.uniforms).to(dev)
+    hist = TokenHistogram.from_csr(w.hist_row_ptr, w.hist_ids, w.hist_counts, dev)
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i: int) -> None:
+        backend.sample_batch(bufs[i % nbuf], params, u, hist, out=out)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    backend.check()
+
+    # CUDA graph of G steps (host launch cost out of the timed region); K = q * G + rem
+    K = args.steps
+    G = min(K, 64)
+    graphs = []
+    for n in ([G] if K % G == 0 else [G, K % G]):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                step(i)
+        graphs.append(g)
+    torch.cuda.synchronize()
+    plan = [graphs[0]] * (K // G) + ([graphs[1]] if K % G else [])
+
+    # per-launch kernel durations: events around single launches with the queue backed up
+    torch.cuda._sleep(50_000_000)
+    pairs = []
+    for i in range(32):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        step(i)
+        e.record(stream)
+        pairs.append((s, e))
+    torch.cuda.synchronize()
+    kernel_ms = statistics.mean(s.elapsed_time(e) for s, e in pairs)
+
+    clocks = Clocks(0)
+    clocks.start()
+    t_end = time.time() + 0.6  # identical load before the timed region, for the clock samples
+    while time.time() < t_end:
+        for g in graphs[:1]:
+            g.replay()
+        torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for g in plan:
+        g.replay()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    total_ms = t0.elapsed_time(t1)
+    t_end = time.time() + 0.4
+    while time.time() < t_end:
+        graphs[0].replay()
+        torch.cuda.synchronize()
+    clk = clocks.stop()
+    backend.check()
+
+    # end to end through the public API: host inputs in, ids out, every step
+    e2e_steps = max(3, min(K, 20))
+    host_logits = w.logits.pin_memory()
+    host_params = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory()
+                   for k, v in w.param_arrays().items()}
+    host_u = torch.from_numpy(w.uniforms).pin_memory()
+    host_hist = [torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+                 for a in (w.hist_row_ptr, w.hist_ids, w.hist_counts)]
+    host_ids = torch.empty(B, dtype=torch.int32).pin_memory()
+    d_logits = torch.empty_like(base)
+    d_params = RowParams.from_arrays(dev, **w.param_arrays())
+    d_u = torch.empty_like(u)
+    d_hist = TokenHistogram(*(torch.empty_like(t, device=dev) for t in host_hist))
+    h2d = (host_logits.numel() * host_logits.element_size() + host_u.numel() * 4
+           + sum(t.numel() * t.element_size() for t in host_params.values())
+           + sum(t.numel() * t.element_size() for t in host_hist))
+
+    def e2e_step() -> None:
+        d_logits.copy_(host_logits, non_blocking=True)
+        for k, t in host_params.items():
+            getattr(d_params, k).copy_(t, non_blocking=True)
+        d_u.copy_(host_u, non_blocking=True)
+        for dst, src in zip((d_hist.row_ptr, d_hist.ids, d_hist.counts), host_hist):
+            dst.copy_(src, non_blocking=True)
+        ids = backend.sample_batch(d_logits, d_params, d_u, d_hist, out=out)
+        host_ids.copy_(ids, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    backend.check()
+    if not np.array_equal(host_ids.numpy(), out.cpu().numpy()):
+        raise RuntimeError("e2e ids differ from the device result")
+
+    peak, peak_kind = measured_peak()
+    algo = w.algorithmic_bytes()
+    achieved = algo / (kernel_ms * 1e-3) / 1e9
+    traffic = ncu_traffic("config3")
+    cpu = None if args.no_cpu_baseline else cpu_reference_rows_per_s(w, args.cpu_seconds)
+    ms_step = total_ms / K
+    return {
+        "metric": "sampled rows/sec (logits HBM GB/s as % of B200 peak in roofline)",
+        "value": B * K / (total_ms * 1e-3),
+        "unit": "rows/s",
+        "n_gpus": 1,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded, configuration 3)",
+        "config": {"workload": "config3: batch 256 x vocab 151936 bf16, rep 1.1 / pres 0.5 / "
+                               "freq 0.3 over 4096-token Zipf(1.1) histories, temp 0.7, "
+                               "top-k 20, top-p 0.8",
+                   "batch": B, "vocab": V, "hist_nnz": w.hist_nnz,
+                   "l2": f"{nbuf} rotating logits buffers "
+                         f"({nbuf * w.logits.numel() * 2 / 2**20:.0f} MiB > 2x L2)",
+                   "parallelism": "single GPU", "graph_steps": G},
+        "gb_per_s": algo / (ms_step * 1e-3) / 1e9,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": f"{peak_kind} (copy bandwidth)",
+                     "traffic": traffic, "algorithmic_bytes": algo,
+                     "kernel": "k_sample<bf16>", "kernel_ms": kernel_ms},
+        "clocks": clk,
+        "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "rows/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": B * 4, "steps": e2e_steps},
+        "gpu_launches": K,
+        "cpu_baseline": cpu,
+    }
+
+
+# ----------------------------------------------------------------------------------------------
+# reference arm: vinfer's CPU sampler on this host
+# ----------------------------------------------------------------------------------------------
+def bench_reference(args, world: int) -> dict:
+    from vinfer_b200.workloads import make  # noqa: PLC0415
+
+    config = 3 if world == 1 else 4
+    w = make(config, batch=None if config == 3 else 64)
+    K, W = args.steps, args.warmup
+    budget = args.ref_seconds
+    t0 = time.perf_counter()
+    est = cpu_reference_rows_per_s(w, 0.0, rows_cap=max(1, min(W, 3)))
+    per_row = 1.0 / est["value"]
+    rows_per_step = max(1, int(budget / max(K, 1) / per_row))
+    cpu_reference_rows_per_s(w, 0.0, rows_cap=max(1, W))  # warm-up steps (1 row each)
+    t1 = time.perf_counter()
+    res = cpu_reference_rows_per_s(w, 0.0, rows_cap=K * rows_per_step)
+    el = time.perf_counter() - t1
+    value = res["value"]
+    return {
+        "impl": "reference",
+        "metric": "sampled rows/sec (logits HBM GB/s as % of B200 peak in roofline)",
+        "value": value,
+        "unit": "rows/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": el * 1e3 / K,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": f"synthetic (seeded, configuration {config})",
+        "config": {"workload": f"config{config}" + ("" if config == 3 else " rows (batch 64 "
+                                                                            "sample, unsharded)"),
+                   "rows_per_step": rows_per_step},
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": res["cores"], "kind": "port",
+                         "sample": res["sample"]},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "wall_s": time.perf_counter() - t0,
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seconds", type=float, default=60.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(bench_reference(args, world)), flush=True)
+        return
+    if world > 1 or args.gpus > 1:
+        from vinfer_b200.sharded import bench_sharded  # noqa: PLC0415
+
+        line = bench_sharded(args)
+    else:
+        line = bench_single(args)
+    if line is not None and rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

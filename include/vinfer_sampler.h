@@ -1,0 +1,125 @@
+/*
+ * vinfer_sampler.h — C ABI of the B200 (sm_100a) token sampler.
+ *
+ * One fused, memory-bound pass per batch of logits rows: repetition / presence / frequency
+ * penalties from per-row token-count histograms, temperature, top-k, softmax, top-p, min-p,
+ * and an inverse-CDF draw from a caller-supplied uniform. A vocab-sharded mode reduces each
+ * rank's shard to a fixed-size candidate record for an all-gather and a merge.
+ *
+ * Every pointer is caller-owned memory. Device pointers unless stated otherwise; no pointer
+ * is retained after a call returns. Calls are stream-ordered on the given CUDA stream
+ * (`void*` is a `cudaStream_t`; NULL is the legacy default stream). Functions return
+ * VINFER_OK or a VINFER_E_* code and never throw; a device-side problem is reported by OR-ing
+ * VINFER_ST_* bits into `*status` (a device int32, may be NULL) and writing -1 as the row's id.
+ *
+ * The entry points replace these reference interfaces (vinfer, pure PyTorch):
+ *   vinfer_sample        <- `sample(logits, params, seed, position) -> int`
+ *                           (src/vinfer/runtime/sampler.py:68-77, called per decode step at
+ *                           src/vinfer/runtime/generate.py:129), batched over rows, and
+ *                           `filtered_probs(logits, params)` (sampler.py:50-65) through
+ *                           the optional `out_probs`.
+ *   vinfer_sampler_workspace_bytes / _init
+ *                        <- per-device workspaces a backend sets up when the engine builds it
+ *                           (src/vinfer/kernels/registry.py:9-11, BackendRegistry.resolve
+ *                           registry.py:84-88 constructs it once).
+ *   vinfer_sample_local / vinfer_sample_merge
+ *                        <- no counterpart: the reference has no distributed code. They are
+ *                           the vocab-sharded form of `vinfer_sample` (logits split along the
+ *                           vocab as a tensor-parallel lm_head produces them,
+ *                           src/vinfer/models/qwen/model.py:230-233).
+ */
+#ifndef VINFER_SAMPLER_H
+#define VINFER_SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VINFER_SAMPLER_ABI_VERSION 1
+
+/* logits element types */
+#define VINFER_DTYPE_F32 0
+#define VINFER_DTYPE_BF16 1
+
+/* return codes */
+#define VINFER_OK 0
+#define VINFER_E_ARG 1      /* a null pointer, a bad size, a dtype or stride out of range */
+#define VINFER_E_LIMIT 2    /* a documented limit exceeded (vocab, batch, workspace too small) */
+#define VINFER_E_CUDA 3     /* a CUDA runtime call failed (launch, attribute) */
+
+/* bits OR-ed into *status by the device */
+#define VINFER_ST_BAD_PARAM 1u   /* a row's parameters are invalid; its id is -1 */
+#define VINFER_ST_NONFINITE 2u   /* a row has no finite maximum after processing */
+#define VINFER_ST_TIMEOUT 4u     /* a bounded wait for a shared-memory copy gave up */
+#define VINFER_ST_INTERNAL 8u    /* an internal consistency check failed */
+
+/* args.flags */
+#define VINFER_FLAG_EXACT_ALL 1u /* resolve every row with the exact multi-pass search */
+
+/* limits */
+#define VINFER_MAX_VOCAB 262144   /* per call (per shard in sharded mode) and in total */
+#define VINFER_MAX_BATCH 65535
+
+typedef struct VinferSampleArgs {
+  const void* logits;          /* [batch, ld] row-major; the first `vocab` columns are used */
+  int32_t dtype;               /* VINFER_DTYPE_F32 or VINFER_DTYPE_BF16 */
+  uint32_t flags;              /* VINFER_FLAG_* */
+  int64_t batch;               /* rows */
+  int64_t vocab;               /* columns processed (the local shard in sharded mode) */
+  int64_t ld;                  /* row stride, in elements (>= vocab) */
+  int64_t vocab_offset;        /* global id of column 0 (0 unless sharded) */
+  int64_t vocab_total;         /* global vocabulary size (== vocab unless sharded) */
+  /* per-row parameters, device float32 / int32 [batch]; NULL selects the default */
+  const float* temperature;    /* 0 = greedy; default 1 */
+  const int32_t* top_k;        /* 0 = off; default 0 */
+  const float* top_p;          /* (0, 1], 1 = off; default 1 */
+  const float* min_p;          /* [0, 1], 0 = off; default 0 */
+  const float* repetition_penalty; /* > 0, 1 = off; default 1 */
+  const float* presence_penalty;   /* 0 = off; default 0 */
+  const float* frequency_penalty;  /* 0 = off; default 0 */
+  /* token-count histograms, CSR over rows, global token ids; NULL row_ptr = no histories */
+  const int64_t* hist_row_ptr; /* [batch + 1] */
+  const int32_t* hist_ids;     /* [nnz], strictly ascending within each row */
+  const int32_t* hist_counts;  /* [nnz]; entries with count <= 0 are ignored */
+  const float* uniforms;       /* [batch] in [0, 1); required unless every row is greedy */
+  int32_t* out_ids;            /* [batch] sampled global token ids */
+  float* out_probs;            /* optional [batch, vocab] final probabilities (parity checks) */
+  int32_t* status;             /* optional, one device int32 */
+} VinferSampleArgs;
+
+/* ABI version of the loaded library (VINFER_SAMPLER_ABI_VERSION). */
+int vinfer_sampler_abi_version(void);
+
+/* Workspace bytes `vinfer_sample` needs for this shape (independent of the device). */
+size_t vinfer_sampler_workspace_bytes(int64_t batch, int64_t vocab, int32_t dtype);
+
+/* Zero a workspace once after allocating it; calls leave it ready for the next call. */
+int vinfer_sampler_workspace_init(void* workspace, size_t bytes, void* stream);
+
+/* Sample one token per row. One workspace serves one call at a time. */
+int vinfer_sample(const VinferSampleArgs* args, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* ---- vocab-sharded mode -------------------------------------------------------------------
+ * Each rank calls vinfer_sample_local on its shard (vocab_offset / vocab_total set), which
+ * writes one fixed-size candidate record per row into `records` (this rank's slice of the
+ * all-gather buffer). After an all-gather of those buffers in rank order, every rank calls
+ * vinfer_sample_merge on the gathered [world][batch] records with identical parameters and
+ * uniforms, and gets identical ids. A row whose cut or draw falls outside the candidates is
+ * marked in `unresolved` (id -1); the caller resolves it with vinfer_sample on the full row.
+ */
+size_t vinfer_sample_record_bytes(int32_t record_cap);  /* bytes of one row's record */
+int vinfer_sample_local(const VinferSampleArgs* args, int32_t record_cap, void* records,
+                        void* workspace, size_t workspace_bytes, void* stream);
+int vinfer_sample_merge(const VinferSampleArgs* args, int32_t record_cap, const void* records,
+                        int32_t world_size, int32_t* unresolved, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VINFER_SAMPLER_H */

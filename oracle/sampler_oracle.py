@@ -179,8 +179,8 @@ def process_row(
     S = e.sum()
     p = e / S
 
-    order = canonical_order(np.where(keep, v, -np.inf).astype(F32))
-    order = order[keep[order]]  # kept-by-top-k tokens, canonical order
+    kept_idx = np.nonzero(keep)[0]  # kept-by-top-k tokens, then canonical order among them
+    order = kept_idx[np.lexsort((kept_idx, -(v64[kept_idx] + 0.0)))]
     ps = p[order]
     n = order.shape[0]
     res = RowResult(token=-1)

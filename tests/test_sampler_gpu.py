@@ -1,0 +1,211 @@
+"""B200 sampler parity against the CPU oracle, through the C ABI (GPU only).
+
+Seeded inputs of the five benchmark configurations at reduced batch but full vocabulary, small
+hand-made vocabularies that reach every branch (ragged tails, ties, -inf, strided and
+misaligned rows, penalties, min-p), the exact multi-pass search checked against the fast
+path, and size-independent properties at the full config-3 batch.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from tests.helpers import compare, oracle_row, run_b200, to_device
+from vinfer_b200 import SAMPLER, BackendContext, SamplingParams, position_uniform
+from vinfer_b200 import _lib
+from vinfer_b200.sampling import RowParams
+from vinfer_b200.workloads import Workload, make
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def backend():
+    return SAMPLER.resolve("b200", BackendContext(torch.device("cuda", 0), torch.bfloat16))
+
+
+def _workload(x: torch.Tensor, params: list[dict], seed: int = 0, hist=None) -> Workload:
+    B = x.shape[0]
+    g = np.random.default_rng(seed)
+
+    def col(name, default, dt=np.float32):
+        return np.array([p.get(name, default) for p in params], dtype=dt)
+
+    w = Workload("custom", x, col("temperature", 1.0), col("top_k", 0, np.int32),
+                 col("top_p", 1.0), col("min_p", 0.0), col("repetition_penalty", 1.0),
+                 col("presence_penalty", 0.0), col("frequency_penalty", 0.0),
+                 g.random(B).astype(np.float32))
+    if hist is not None:
+        w.hist_row_ptr, w.hist_ids, w.hist_counts = hist
+    return w
+
+
+GRID = [
+    {"temperature": 0.0},
+    {"temperature": 1.0},
+    {"temperature": 0.7, "top_k": 1},
+    {"temperature": 0.7, "top_k": 3},
+    {"temperature": 1.3, "top_k": 20},
+    {"temperature": 0.5, "top_p": 0.8},
+    {"temperature": 1.0, "top_p": 0.3},
+    {"temperature": 0.9, "top_k": 50, "top_p": 0.9},
+    {"temperature": 1.0, "min_p": 0.05},
+    {"temperature": 0.6, "top_k": 20, "top_p": 0.95, "min_p": 0.1},
+    {"temperature": 2.0, "top_p": 0.999},
+    {"temperature": 0.2, "top_k": 300},
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=str)
+@pytest.mark.parametrize("V", [6, 7, 96, 1000, 4097, 40000])
+def test_small_vocabularies_match_the_oracle(backend, V, dtype):
+    g = torch.Generator().manual_seed(V)
+    B = len(GRID)
+    x = (torch.randn(B, V, generator=g) * 2.0).to(dtype)
+    w = _workload(x, GRID, seed=V)
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=str)
+def test_penalties_match_the_oracle(backend, dtype):
+    V = 5000
+    g = torch.Generator().manual_seed(7)
+    params = [dict(p, repetition_penalty=1.3, presence_penalty=0.4, frequency_penalty=0.2)
+              for p in GRID]
+    B = len(params)
+    x = (torch.randn(B, V, generator=g) * 2.0).to(dtype)
+    rng = np.random.default_rng(1)
+    rows = []
+    for r in range(B):
+        # the top logits are the most likely to be penalised, so the penalties change ranks
+        top = torch.topk(x[r].float(), 40).indices.numpy()
+        rows.append(np.concatenate([top[::2], rng.integers(0, V, 200)]))
+    ptr, ids_, cnt = [0], [], []
+    for t in rows:
+        u, c = np.unique(t, return_counts=True)
+        ids_.append(u.astype(np.int32))
+        cnt.append(c.astype(np.int32))
+        ptr.append(ptr[-1] + len(u))
+    w = _workload(x, params, hist=(np.array(ptr), np.concatenate(ids_), np.concatenate(cnt)))
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+@pytest.mark.parametrize("config,batch", [(1, None), (2, 24), (3, 16), (5, 16)])
+def test_benchmark_configs_match_the_oracle(backend, config, batch):
+    w = make(config, batch=batch)
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    print(f"config {config}: {rep}")
+    assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+def test_config5_every_row_class(backend):
+    w = make(5, batch=32)  # eight rows of each class: flat, dominant, 1000-way tie, normal
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    print(f"config 5 classes: {rep}")
+    assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+@pytest.mark.parametrize("config,batch", [(2, 24), (3, 16)])
+def test_exact_search_agrees_with_the_fast_path(backend, config, batch):
+    w = make(config, batch=batch)
+    ids_fast, p_fast = run_b200(backend, w)
+    ids_exact, p_exact = run_b200(backend, w, exact=True)
+    same = ids_fast == ids_exact
+    for r in np.nonzero(~same)[0]:
+        assert oracle_row(w, int(r)).boundary, f"row {r}: fast {ids_fast[r]} exact {ids_exact[r]}"
+    np.testing.assert_allclose(p_exact, p_fast, rtol=2e-5, atol=1e-30)
+
+
+def test_ties_flat_rows_and_masked_logits(backend):
+    V = 3000
+    x = torch.randn(8, V, generator=torch.Generator().manual_seed(3))
+    x[0] = 0.5  # flat
+    x[1, :] = -1.0
+    x[1, 100:400] = 2.0  # 300-way tie at the max
+    x[2, 1::2] = float("-inf")  # masked half of the vocabulary
+    x[3, :] = -0.0
+    x[3, ::3] = 0.0  # signed zeros compare equal
+    x[4, 10] = 40.0  # one dominant token
+    x[5, 2500:] = float("-inf")
+    x[6, ::7] = 3.0
+    params = [{"temperature": 1.0, "top_p": 0.37}, {"temperature": 0.8, "top_k": 5},
+              {"temperature": 1.0, "top_k": 10}, {"temperature": 1.0, "top_p": 0.5},
+              {"temperature": 0.5, "top_p": 0.9}, {"temperature": 1.0, "top_k": 2999},
+              {"temperature": 1.0, "top_k": 100, "top_p": 0.6}, {"temperature": 0.0}]
+    for dtype in (torch.float32, torch.bfloat16):
+        w = _workload(x.to(dtype), params, seed=5)
+        for exact in (False, True):
+            ids, probs = run_b200(backend, w, exact=exact)
+            rep = compare(w, ids, probs)
+            assert not rep.failures, (dtype, exact, str(rep), rep.failures[:5])
+
+
+def test_strided_and_misaligned_rows(backend):
+    w = make(2, batch=8, vocab=20001)
+    ids_ref, _ = run_b200(backend, w, probs=False)
+    for dtype in (torch.bfloat16, torch.float32):
+        w2 = make(2, batch=8, vocab=20001)
+        w2.logits = w2.logits.to(dtype)
+        ids_c, _ = run_b200(backend, w2, probs=False)
+        if dtype == torch.bfloat16:
+            np.testing.assert_array_equal(ids_c, ids_ref)
+        # rows with a larger stride, starting 1..3 elements past an aligned address
+        for shift in (1, 3):
+            big = torch.full((8, 20001 + 37), float("nan"), dtype=dtype, device=backend.device)
+            big[:, shift:shift + 20001] = w2.logits.to(backend.device)
+            view = big[:, shift:shift + 20001]
+            ids_v, _ = run_b200(backend, w2, probs=False, logits=view)
+            np.testing.assert_array_equal(ids_v, ids_c)
+
+
+def test_full_batch_config3_is_deterministic_and_valid(backend):
+    w = make(3)
+    lg, params, u, hist = to_device(w, backend.device)
+    a = backend.sample_batch(lg, params, u, hist).cpu().numpy()
+    b = backend.sample_batch(lg, params, u, hist).cpu().numpy()
+    backend.check()
+    np.testing.assert_array_equal(a, b)
+    assert ((a >= 0) & (a < w.vocab)).all()
+    rep = compare(w, a, None, rows=list(range(0, 256, 32)))
+    assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+def test_single_row_api_uses_the_position_uniform(backend):
+    w = make(1)
+    x = w.logits[0].to(backend.device)
+    p = SamplingParams(temperature=0.7, top_k=20, top_p=0.8)
+    for pos in range(20):
+        tok = backend.sample(x, p, seed=11, position=pos)
+        w.uniforms[0] = np.float32(position_uniform(11, pos))
+        w.hist_row_ptr = None
+        w.repetition_penalty[0] = 1.0
+        res = oracle_row(w, 0)
+        assert res.boundary or tok == res.token
+
+
+def test_invalid_row_parameters_are_reported(backend):
+    V = 100
+    x = torch.randn(3, V, device=backend.device)
+    params = RowParams.from_arrays(backend.device, temperature=np.array([1.0, 1.0, -1.0]),
+                                   top_p=np.array([1.0, 0.0, 1.0]))
+    u = torch.full((3,), 0.5, device=backend.device)
+    ids = backend.sample_batch(x, params, u).cpu().numpy()
+    assert ids[0] >= 0 and ids[1] == -1 and ids[2] == -1
+    with pytest.raises(RuntimeError, match="invalid sampling parameters"):
+        backend.check()
+
+
+def test_host_side_argument_errors_do_not_launch(backend):
+    x = torch.randn(2, 10, device=backend.device)
+    params = RowParams.from_arrays(backend.device, temperature=np.array([1.0]))
+    with pytest.raises(ValueError):
+        backend.sample_batch(x, params, torch.zeros(2, device=backend.device))
+    assert _lib.load().vinfer_sample(None, None, 0, None) == _lib.E_ARG
