@@ -48,7 +48,9 @@ def test_struct_layout_matches_the_header():
 def test_workspace_sizes(lib):
     a = lib.vinfer_sampler_workspace_bytes(256, 151936, _lib.DTYPE_BF16)
     b = lib.vinfer_sampler_workspace_bytes(256, 151936, _lib.DTYPE_F32)
-    assert 0 < a < b < 256 << 20
+    assert 0 < a <= b < 256 << 20
+    big = lib.vinfer_sampler_workspace_bytes(4096, 151936, _lib.DTYPE_F32)
+    assert b < big < 4 << 30
     assert lib.vinfer_sampler_workspace_bytes(0, 100, _lib.DTYPE_F32) == 0
     assert lib.vinfer_sampler_workspace_bytes(1, _lib.MAX_VOCAB + 1, _lib.DTYPE_F32) == 0
     assert lib.vinfer_sampler_workspace_bytes(1, 100, 7) == 0

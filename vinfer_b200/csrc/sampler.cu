@@ -6,23 +6,27 @@
 // repetition / presence / frequency penalties, min-p and an inverse-CDF draw from a caller
 // uniform. Tokens are ordered canonically: descending processed logit, ties by ascending id.
 //
-// Layout and passes (one launch of k_sample per batch):
-//   * The grid is (segments, rows). A CTA owns one contiguous segment of one row (<= 32 KiB of
-//     logits), copies it HBM -> shared memory with one TMA bulk copy, and reads HBM nowhere
-//     else on the fast path.
-//   * Penalised tokens of the segment (the row's CSR histogram entries in range) are taken out
-//     of the resident copy (set to -inf) and kept as a side list of exact float32 values.
-//   * One pass over shared memory computes, per group of 16 bytes x 2 vectors, the group
-//     maximum, and (top-k off) an online softmax max/sum. The K-th largest group maximum is a
-//     lower bound of the K-th largest value, so only groups at or above it are rescanned to
-//     collect candidates; an exact radix select on them gives the segment's top-K with all
-//     ties. The segment record (candidates, max, sum, completeness threshold) goes to the
-//     workspace.
-//   * The last CTA of a row to finish (threadfence + atomic counter) merges the records:
-//     bitonic sort into canonical order, top-k, top-p and min-p cuts by prefix sums, and the
-//     draw. A row whose cut or draw lies below what the records hold completely, or whose
-//     candidates overflowed, is finished by an exact multi-pass search over the row (radix
-//     histograms of mass in 2^-44 fixed point, ties resolved in id order) in the same CTA.
+// Execution (one launch of k_sample per batch):
+//   * Work items are (row, segment) pairs; a segment is <= 32 KiB of one row's logits. The grid
+//     is persistent (two CTAs per SM): CTA b takes items b, b + grid, b + 2 grid, ...
+//   * Each CTA has two producer warps and eight consumer warps. Producer warp p owns shared
+//     stage p: it reads the row's parameters, finds the segment's slice of the row's sorted
+//     history (warp-cooperative search), loads those entries and the unaligned edges, then
+//     copies the 16-byte-aligned interior of the segment HBM -> shared memory with one TMA bulk
+//     copy per 16 KiB on an mbarrier. Metadata for the next item is fetched before the stage
+//     is free, so the consumers find each stage full when they get to it.
+//   * Consumers take penalised tokens out of the staged copy (exact float32 side values), make
+//     one pass computing per-thread maxima (plus an online softmax sum when top-k is off),
+//     extract the K largest per-thread maxima per warp (K distinct elements, so their K-th
+//     largest bounds the segment's K-th largest value from below), collect every element at or
+//     above that bound, rank the candidates by counting and write the top K with all ties,
+//     sorted, as the segment's record.
+//   * The CTA that completes a row's last record (acq_rel atomic counter, result consumed one
+//     item later so its latency is hidden) merges the row: sorted records -> merged by rank,
+//     top-k, top-p and min-p cuts by prefix sums, and the draw. A row whose cut or draw lies
+//     below what the records hold completely, or whose candidates overflowed, is finished by an
+//     exact multi-pass search over the row (radix histograms of mass in 2^-44 fixed point, ties
+//     resolved in id order) in the same CTA.
 //
 // All reductions run in a fixed order, so results are deterministic run to run.
 
@@ -41,30 +45,35 @@ namespace {
 // ---------------------------------------------------------------------------------------------
 // configuration
 // ---------------------------------------------------------------------------------------------
-constexpr int NT = 256;                 // threads per CTA
-constexpr int NWARP = NT / 32;
-constexpr int SEG_BYTES = 32768;        // largest segment held in shared memory
+constexpr int NCW = 8;                  // consumer warps
+constexpr int NT = NCW * 32;            // consumer threads
+constexpr int NSTAGE = 2;               // shared-memory stages
+constexpr int NTHR = NT + 32;           // threads per CTA: consumers + one producer warp
+constexpr int SEG_BYTES = 32768;        // largest segment held in a stage
 constexpr int SBUF_BYTES = SEG_BYTES + 64;
-constexpr int CAND_CAP = 1024;          // candidates collected per segment
-constexpr int SIDE_CAP = 2048;          // penalised tokens per segment
+constexpr int SIDE_CAP = 512;           // penalised tokens per segment
+constexpr int SIDE_PER_LANE = SIDE_CAP / 32;
+constexpr int CAND_CAP = 1024;          // entries of one record
+constexpr int RUN_CAP = 2048;           // candidates held for the run being processed
+constexpr int CTA_CAP = 320;            // resident CTAs assumed when sizing workspaces
 constexpr int KMAX = 256;               // largest top-k served by the candidate path
-constexpr int KC = 128;                 // candidates kept per segment when top-k is off
-constexpr int MAX_NSEG = 32;
-constexpr int GROUP_VECS = 2;           // 16-byte vectors per group
-constexpr int MAX_VEC = SBUF_BYTES / 16;
-constexpr int MAX_R = (MAX_VEC + NT - 1) / NT;
-constexpr int MAX_GSLOT = ((MAX_R + GROUP_VECS - 1) / GROUP_VECS) * NT;
-constexpr int SIDE_GROUP = 8;
-constexpr int MAX_SGROUP = SIDE_CAP / SIDE_GROUP;
-constexpr int MERGE_CAP = SBUF_BYTES / 8 / 2 * 2 >= 4096 ? 4096 : 0;
-constexpr int BM_WORDS = SEG_BYTES / 2 / 32 + 8;
-constexpr int FB_BINS = 2048;           // radix bins of the exact search (11 + 11 + 10 bits)
+constexpr int KC = 64;                  // candidates kept per segment when top-k is off
+constexpr int MAX_NSEG = 64;
+constexpr int MERGE_CAP = 2048;         // merged entries (input in cand, sorted copy in a stage)
+constexpr int BM_WORDS = (SBUF_BYTES / 2 + 31) / 32 + 2;
 constexpr float LOG2E = 1.4426950408889634f;
-constexpr double FX_ONE = 17592186044416.0;  // 2^44: fixed-point unit of probability mass
+constexpr double FX_ONE = 17592186044416.0;      // 2^44: fixed-point unit of probability mass
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz: bound on any wait
+constexpr unsigned FULLMASK = 0xffffffffu;
 
-static_assert(MERGE_CAP == 4096, "merge buffer must hold 4096 entries");
-static_assert((size_t)VINFER_MAX_VOCAB / 8 <= (size_t)SBUF_BYTES, "row bitmap must fit");
+static_assert(NT == 256, "block helpers assume 256 consumer threads");
+static_assert(KMAX <= 8 * 32, "warp extraction covers at most 8 x 32 values");
+static_assert(MERGE_CAP * 8 <= SEG_BYTES, "a stage holds the sorted merge");
+static_assert((int64_t)VINFER_MAX_VOCAB * 4 <= (int64_t)MAX_NSEG * SEG_BYTES,
+              "the largest float32 row fits MAX_NSEG segments");
+static_assert(MERGE_CAP <= RUN_CAP, "the candidate buffer holds the merge input");
+static_assert((size_t)VINFER_MAX_VOCAB / 8 <= (size_t)RUN_CAP * 8 + SEG_BYTES,
+              "the exact search's row bitmap spans the candidate buffer and a stage");
 
 // record flags
 constexpr uint32_t REC_UNRETAINED = 1u;  // elements below t_key exist that are not listed
@@ -76,7 +85,7 @@ struct RecHdr {
   float m_y;        // largest penalised logit of the source (pre-temperature)
   float s;          // sum of exp2((y - m_y) * log2(e) / T) over the source (top-k off only)
   uint32_t t_key;   // every element with key >= t_key is listed
-  int32_t n;        // listed entries
+  int32_t n;        // listed entries, sorted ascending by composite key (= canonical order)
   uint32_t flags;
   int32_t pad[3];
 };
@@ -98,7 +107,8 @@ constexpr size_t REC_STRIDE = sizeof(RecHdr) + 8 * CAND_CAP;
 struct KParams {
   const void* logits;
   int64_t ld, V, voff, vtotal;
-  int B, nseg, seg_len, mode;  // mode 0: finalize, 1: local (write shard records)
+  int B, nseg, seg_len, mode;  // mode 0: finalize, 1: local (write shard records), 2: merge
+  int total, grid;             // segments in the batch (B * nseg) and CTAs sharing them
   uint32_t flags;
   const float* temperature;
   const int* top_k;
@@ -122,23 +132,39 @@ struct KParams {
   size_t shard_stride;
 };
 
-// shared memory of k_sample; the merge and the exact search reuse the same bytes
-struct __align__(16) Smem {
-  unsigned char sbuf[SBUF_BYTES];             // segment / merge entries / row bitmap
-  uint32_t gkey[MAX_GSLOT + MAX_SGROUP];      // group maxima (keys)
-  uint32_t ckey[CAND_CAP];                    // candidate keys    } exact search: counts
-  int32_t cid[CAND_CAP];                      // candidate ids     }
-  int32_t side_li[SIDE_CAP];                  // penalised: local index } exact search: masses
-  float side_y[SIDE_CAP];                     // penalised: value       }
-  uint32_t bitmap[BM_WORDS];                  // penalised positions of the segment
-  uint32_t hist[256];
-  unsigned long long red64[NWARP + 1];
-  float redf[2 * NWARP + 2];
-  int32_t redi[NWARP + 2];
-  int32_t sc[16];
-  float sf[8];
-  unsigned long long mbar;
+struct __align__(16) Stage {
+  unsigned char data[SBUF_BYTES];  // the segment; merge / exact search scratch afterwards
+  int32_t side_id[SIDE_CAP];       // penalised tokens of the segment (global ids) ...
+  int32_t side_cnt[SIDE_CAP];      // ... and their counts
+  float prm[8];                    // T, top_p, min_p, rep, pres, freq, uniform, top_k (bits)
+  int32_t ns;                      // side entries, -1 when more than SIDE_CAP
+  int32_t pad[3];
 };
+
+struct __align__(16) Smem {
+  Stage st[NSTAGE];
+  unsigned long long cand[RUN_CAP];   // candidates of the run (composite keys); exact: bins
+  float side_y[SIDE_CAP];             // penalised values of the current item
+  uint32_t bitmap[BM_WORDS];          // penalised slots of the current item
+  float ext[NT];                      // lane maxima extracted per warp
+  unsigned long long bin_mass[256];   // exact search: radix bins
+  uint32_t bin_cnt[256];
+  RecHdr mh[MAX_NSEG];
+  int moff[MAX_NSEG + 1];
+  unsigned long long red64[NCW + 1];
+  float redf[NCW + 1];
+  int redi[NCW + 1];
+  int sc[16];
+  float sf[8];
+  unsigned long long full[NSTAGE];
+  unsigned long long empty[NSTAGE];
+};
+
+// scalar slots in Smem::sc / Smem::sf
+enum { SC_NC = 0, SC_NRET, SC_TKEY, SC_LAST, SC_B, SC_J, SC_X0, SC_X1, SC_NQ, SC_RFL };
+// run flags in Smem::sc[SC_RFL]
+constexpr int RUN_OVER = 1;  // a side list or the candidate buffer overflowed
+enum { SF_TH = 0, SF_YLO, SF_SK, SF_M };
 
 // ---------------------------------------------------------------------------------------------
 // small device helpers
@@ -169,17 +195,40 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ void status_or(const KParams& P, uint32_t bits) {
   if (P.status) atomicOr(reinterpret_cast<unsigned int*>(P.status), bits);
 }
+// barrier of the consumer warps only (the producer warps run their own loop)
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
+__device__ __forceinline__ bool cbar_or(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred a, b;\n setp.ne.u32 a, %1, 0;\n bar.red.or.pred b, 1, %2, a;\n"
+      " selp.u32 %0, 1, 0, b;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)p), "n"(NT)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
 
 // ---- TMA bulk copy (global -> shared) with an mbarrier, waits bounded -----------------------
 __device__ __forceinline__ void mbar_init(unsigned long long* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
                : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
-__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, uint32_t bytes) {
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)
                : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes,
                                             unsigned long long* bar) {
@@ -200,7 +249,9 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t 
   return ok != 0;
 }
 // Wait for phase `parity` of `bar`, giving up after WAIT_CYCLES. Returns false on timeout.
+// try_wait suspends the warp in hardware until the phase completes or a short time limit.
 __device__ bool mbar_wait_bounded(unsigned long long* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (clock64() - t0 > WAIT_CYCLES) return false;
@@ -215,11 +266,12 @@ template <>
 struct Elem<float> {
   static constexpr int A = 4;  // elements per 16 bytes
   __device__ static float ld(const void* p, int64_t i) { return __ldg((const float*)p + i); }
+  __device__ static uint32_t ldraw(const void* p, int64_t i) {
+    return __ldg((const unsigned int*)p + i);
+  }
+  __device__ static void straw(void* s, int i, uint32_t v) { ((uint32_t*)s)[i] = v; }
   __device__ static float sm(const void* s, int i) { return ((const float*)s)[i]; }
   __device__ static void neg_inf(void* s, int i) { ((uint32_t*)s)[i] = 0xFF800000u; }
-  __device__ static void copy(void* s, int i, const void* p, int64_t j) {
-    ((float*)s)[i] = __ldg((const float*)p + j);
-  }
   __device__ static float vmax(const uint4& q) {
     return fmaxf(fmaxf(__uint_as_float(q.x), __uint_as_float(q.y)),
                  fmaxf(__uint_as_float(q.z), __uint_as_float(q.w)));
@@ -236,13 +288,16 @@ struct Elem<__nv_bfloat16> {
     const unsigned short b = __ldg((const unsigned short*)p + i);
     return __uint_as_float((uint32_t)b << 16);
   }
+  __device__ static uint32_t ldraw(const void* p, int64_t i) {
+    return __ldg((const unsigned short*)p + i);
+  }
+  __device__ static void straw(void* s, int i, uint32_t v) {
+    ((unsigned short*)s)[i] = (unsigned short)v;
+  }
   __device__ static float sm(const void* s, int i) {
     return __uint_as_float((uint32_t)((const unsigned short*)s)[i] << 16);
   }
   __device__ static void neg_inf(void* s, int i) { ((unsigned short*)s)[i] = 0xFF80u; }
-  __device__ static void copy(void* s, int i, const void* p, int64_t j) {
-    ((unsigned short*)s)[i] = __ldg((const unsigned short*)p + j);
-  }
   __device__ static float vmax(const uint4& q) {
     const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&q.x);
     const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&q.y);
@@ -257,6 +312,33 @@ struct Elem<__nv_bfloat16> {
   }
 };
 
+// segment geometry: local index i lives at slot off + i of the stage buffer
+struct Geo {
+  int64_t lo, gbase;
+  int n, head, inter, tail0, off, nvec, pad_end;
+  const void* rowp;
+};
+template <typename TIn>
+__device__ Geo geometry(const KParams& P, int row, int seg) {
+  constexpr int A = Elem<TIn>::A;
+  constexpr int ES = 16 / A;
+  Geo g;
+  g.lo = (int64_t)seg * P.seg_len;
+  const int64_t hi = min(P.V, g.lo + (int64_t)P.seg_len);
+  g.n = (int)(hi - g.lo);
+  g.rowp = (const TIn*)P.logits + (int64_t)row * P.ld;
+  const uintptr_t gaddr = (uintptr_t)((const TIn*)g.rowp + g.lo);
+  g.head = (int)(((16u - (uint32_t)(gaddr & 15u)) & 15u) / ES);
+  if (g.head > g.n) g.head = g.n;
+  g.inter = (int)((((int64_t)(g.n - g.head) * ES) / 16) * 16 / ES);
+  g.tail0 = g.head + g.inter;
+  g.off = (A - g.head % A) % A;
+  g.nvec = (g.off + g.n + A - 1) / A;
+  g.pad_end = g.nvec * A - (g.off + g.n);
+  g.gbase = P.voff + g.lo;
+  return g;
+}
+
 // ---------------------------------------------------------------------------------------------
 // per-row configuration
 // ---------------------------------------------------------------------------------------------
@@ -266,30 +348,54 @@ struct RowCfg {
   bool greedy, topk, need_sum, pen, bad, exact;
 };
 
-__device__ RowCfg load_row(const KParams& P, int row) {
+__device__ RowCfg make_cfg(const KParams& P, float T, int k, float p, float minp, float rep,
+                           float pres, float freq, float u) {
   RowCfg c;
-  c.T = P.temperature ? P.temperature[row] : 1.f;
-  c.k = P.top_k ? P.top_k[row] : 0;
-  c.p = P.top_p ? P.top_p[row] : 1.f;
-  c.minp = P.min_p ? P.min_p[row] : 0.f;
-  c.rep = P.rep ? P.rep[row] : 1.f;
-  c.pres = P.pres ? P.pres[row] : 0.f;
-  c.freq = P.freq ? P.freq[row] : 0.f;
-  c.u = P.uni ? P.uni[row] : 0.f;
-  c.greedy = (c.T == 0.f);
-  bool bad = !(c.T >= 0.f && c.T <= FLT_MAX) || !(c.p > 0.f && c.p <= 1.f) || c.k < 0 ||
-             !(c.minp >= 0.f && c.minp <= 1.f) || !(c.rep > 0.f && c.rep <= FLT_MAX) ||
-             !(fabsf(c.pres) <= FLT_MAX) || !(fabsf(c.freq) <= FLT_MAX);
-  if (!c.greedy) bad = bad || P.uni == nullptr || !(c.u >= 0.f && c.u < 1.f);
+  c.T = T;
+  c.k = k;
+  c.p = p;
+  c.minp = minp;
+  c.rep = rep;
+  c.pres = pres;
+  c.freq = freq;
+  c.u = u;
+  c.greedy = (T == 0.f);
+  bool bad = !(T >= 0.f && T <= FLT_MAX) || !(p > 0.f && p <= 1.f) || k < 0 ||
+             !(minp >= 0.f && minp <= 1.f) || !(rep > 0.f && rep <= FLT_MAX) ||
+             !(fabsf(pres) <= FLT_MAX) || !(fabsf(freq) <= FLT_MAX);
+  if (!c.greedy) bad = bad || P.uni == nullptr || !(u >= 0.f && u < 1.f);
   c.bad = bad;
-  c.topk = !c.greedy && c.k > 0 && (int64_t)c.k < P.vtotal;
-  c.K = c.greedy ? 1 : (c.topk ? c.k : KC);
+  c.topk = !c.greedy && k > 0 && (int64_t)k < P.vtotal;
+  c.K = c.greedy ? 1 : (c.topk ? k : KC);
   c.need_sum = !c.greedy && !c.topk;
-  c.exact = (P.flags & VINFER_FLAG_EXACT_ALL) != 0 || (c.topk && c.k > KMAX);
-  c.c2 = c.greedy ? 0.f : __fdiv_rn(LOG2E, c.T);
-  c.lm = c.minp > 0.f ? log2f(c.minp) : -INFINITY;
-  c.pen = P.hrow != nullptr && (c.rep != 1.f || c.pres != 0.f || c.freq != 0.f);
+  c.exact = (P.flags & VINFER_FLAG_EXACT_ALL) != 0 || (c.topk && k > KMAX);
+  c.c2 = c.greedy ? 0.f : __fdiv_rn(LOG2E, T);
+  c.lm = minp > 0.f ? log2f(minp) : -INFINITY;
+  c.pen = P.hrow != nullptr && (rep != 1.f || pres != 0.f || freq != 0.f);
   return c;
+}
+// parameter `i` of a row: 0 T, 1 top_p, 2 min_p, 3 rep, 4 pres, 5 freq, 6 uniform, 7 top_k bits
+__device__ float load_param(const KParams& P, int row, int i) {
+  switch (i) {
+    case 0: return P.temperature ? __ldg(P.temperature + row) : 1.f;
+    case 1: return P.top_p ? __ldg(P.top_p + row) : 1.f;
+    case 2: return P.min_p ? __ldg(P.min_p + row) : 0.f;
+    case 3: return P.rep ? __ldg(P.rep + row) : 1.f;
+    case 4: return P.pres ? __ldg(P.pres + row) : 0.f;
+    case 5: return P.freq ? __ldg(P.freq + row) : 0.f;
+    case 6: return P.uni ? __ldg(P.uni + row) : 0.f;
+    default: return __int_as_float(P.top_k ? __ldg(P.top_k + row) : 0);
+  }
+}
+__device__ RowCfg cfg_from(const KParams& P, const float* prm) {
+  return make_cfg(P, prm[0], __float_as_int(prm[7]), prm[1], prm[2], prm[3], prm[4], prm[5],
+                  prm[6]);
+}
+__device__ RowCfg load_row(const KParams& P, int row) {
+  float prm[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) prm[i] = load_param(P, row, i);
+  return cfg_from(P, prm);
 }
 
 // penalties: repetition, then frequency * count, then presence; one IEEE op each
@@ -302,19 +408,7 @@ __device__ __forceinline__ float penalize(float x, int cnt, const RowCfg& c) {
 __device__ __forceinline__ float vf(float y, const RowCfg& c) {
   return c.greedy ? y : __fdiv_rn(y, c.T);
 }
-// smallest y with vf(y) >= vt, given vf(yhi) >= vt (binary search over ordered keys)
-__device__ float preimage_lo(float vt, float yhi, const RowCfg& c) {
-  if (c.greedy || vt == -INFINITY) return vt;
-  uint32_t lo = okey(-INFINITY), hi = okey(yhi);
-  if (vf(from_okey(lo), c) >= vt) return -INFINITY;
-  while (hi - lo > 1) {
-    const uint32_t mid = lo + (hi - lo) / 2;
-    if (vf(from_okey(mid), c) >= vt) hi = mid; else lo = mid;
-  }
-  return from_okey(hi);
-}
-
-// first index >= target in the ascending ids[a, b)
+// first index >= target in the ascending ids[a, b) (one thread)
 __device__ int64_t lower_bound_ids(const int* ids, int64_t a, int64_t b, int64_t target) {
   while (a < b) {
     const int64_t mid = a + (b - a) / 2;
@@ -322,436 +416,133 @@ __device__ int64_t lower_bound_ids(const int* ids, int64_t a, int64_t b, int64_t
   }
   return a;
 }
+// the same, by a whole warp: 32 probes per round, so about two dependent loads per search
+__device__ int64_t warp_lower_bound(const int* ids, int64_t a, int64_t b, int64_t target,
+                                    int lane) {
+  while (b - a > 32) {
+    const int64_t step = (b - a + 31) / 32;
+    const int64_t p = a + lane * step;
+    const bool lt = p < b && (int64_t)__ldg(ids + p) < target;
+    const int c = __popc(__ballot_sync(FULLMASK, lt));
+    if (c == 0) return a;
+    const int64_t na = a + (int64_t)(c - 1) * step + 1;
+    b = min(b, a + (int64_t)c * step);
+    a = na;
+  }
+  const int64_t p = a + lane;
+  const bool lt = p < b && (int64_t)__ldg(ids + p) < target;
+  return a + __popc(__ballot_sync(FULLMASK, lt));
+}
 
 // ---------------------------------------------------------------------------------------------
-// block-wide building blocks (all threads of the CTA call them)
+// consumer-wide building blocks (all 256 consumer threads call them)
 // ---------------------------------------------------------------------------------------------
-// exclusive scan of one float per thread, in thread order; returns the total too
-__device__ float block_excl_scan_f(float x, float* total, Smem& S) {
+__device__ float cta_excl_scan_f(float x, float* total, Smem& S) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   float inc = x;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const float t = __shfl_up_sync(0xffffffffu, inc, o);
+    const float t = __shfl_up_sync(FULLMASK, inc, o);
     if (lane >= o) inc += t;
   }
-  __syncthreads();
+  cbar();
   if (lane == 31) S.redf[w] = inc;
-  __syncthreads();
+  cbar();
   if (threadIdx.x == 0) {
     float run = 0.f;
-    for (int i = 0; i < NWARP; ++i) {
+    for (int i = 0; i < NCW; ++i) {
       const float t = S.redf[i];
       S.redf[i] = run;
       run += t;
     }
-    S.redf[NWARP] = run;
+    S.redf[NCW] = run;
   }
-  __syncthreads();
-  const float r = S.redf[w] + inc - x;
-  *total = S.redf[NWARP];
-  return r;
+  cbar();
+  *total = S.redf[NCW];
+  return S.redf[w] + inc - x;
 }
-__device__ unsigned long long block_excl_scan_u64(unsigned long long x, unsigned long long* total,
-                                                  Smem& S) {
+__device__ unsigned long long cta_excl_scan_u64(unsigned long long x, unsigned long long* total,
+                                                Smem& S) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   unsigned long long inc = x;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const unsigned long long t = __shfl_up_sync(0xffffffffu, inc, o);
+    const unsigned long long t = __shfl_up_sync(FULLMASK, inc, o);
     if (lane >= o) inc += t;
   }
-  __syncthreads();
+  cbar();
   if (lane == 31) S.red64[w] = inc;
-  __syncthreads();
+  cbar();
   if (threadIdx.x == 0) {
     unsigned long long run = 0;
-    for (int i = 0; i < NWARP; ++i) {
+    for (int i = 0; i < NCW; ++i) {
       const unsigned long long t = S.red64[i];
       S.red64[i] = run;
       run += t;
     }
-    S.red64[NWARP] = run;
+    S.red64[NCW] = run;
   }
-  __syncthreads();
-  const unsigned long long r = S.red64[w] + inc - x;
-  *total = S.red64[NWARP];
-  return r;
+  cbar();
+  *total = S.red64[NCW];
+  return S.red64[w] + inc - x;
 }
-__device__ int block_excl_scan_i(int x, int* total, Smem& S) {
+__device__ int cta_excl_scan_i(int x, int* total, Smem& S) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   int inc = x;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const int t = __shfl_up_sync(0xffffffffu, inc, o);
+    const int t = __shfl_up_sync(FULLMASK, inc, o);
     if (lane >= o) inc += t;
   }
-  __syncthreads();
+  cbar();
   if (lane == 31) S.redi[w] = inc;
-  __syncthreads();
+  cbar();
   if (threadIdx.x == 0) {
     int run = 0;
-    for (int i = 0; i < NWARP; ++i) {
+    for (int i = 0; i < NCW; ++i) {
       const int t = S.redi[i];
       S.redi[i] = run;
       run += t;
     }
-    S.redi[NWARP] = run;
+    S.redi[NCW] = run;
   }
-  __syncthreads();
-  const int r = S.redi[w] + inc - x;
-  *total = S.redi[NWARP];
-  return r;
+  cbar();
+  *total = S.redi[NCW];
+  return S.redi[w] + inc - x;
 }
-__device__ unsigned long long block_min_u64(unsigned long long x, Smem& S) {
+__device__ unsigned long long cta_min_u64(unsigned long long x, Smem& S) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long t = __shfl_xor_sync(0xffffffffu, x, o);
+    const unsigned long long t = __shfl_xor_sync(FULLMASK, x, o);
     x = t < x ? t : x;
   }
-  __syncthreads();
+  cbar();
   if ((threadIdx.x & 31) == 0) S.red64[threadIdx.x >> 5] = x;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned long long m = S.red64[0];
-    for (int i = 1; i < NWARP; ++i) m = S.red64[i] < m ? S.red64[i] : m;
-    S.red64[NWARP] = m;
-  }
-  __syncthreads();
-  return S.red64[NWARP];
+  cbar();
+  unsigned long long m = S.red64[0];
+  for (int i = 1; i < NCW; ++i) m = S.red64[i] < m ? S.red64[i] : m;
+  return m;
 }
-__device__ uint32_t block_max_u32(uint32_t x, Smem& S) {
-  unsigned long long y = ~(unsigned long long)x;  // max via min of complements
-  return (uint32_t)~block_min_u64(y, S);
+__device__ uint32_t cta_max_u32(uint32_t x, Smem& S) {
+  return (uint32_t)~cta_min_u64(~(unsigned long long)x, S);
 }
-__device__ unsigned long long block_sum_u64(unsigned long long x, Smem& S) {
+__device__ unsigned long long cta_sum_u64(unsigned long long x, Smem& S) {
   unsigned long long tot;
-  block_excl_scan_u64(x, &tot, S);
+  cta_excl_scan_u64(x, &tot, S);
   return tot;
-}
-
-// K-th largest of keys[0, n) (1 <= K <= n): exact radix select, 8-bit digits from the top.
-// *rank_in_ties receives how many elements equal to the result are needed to reach K.
-__device__ uint32_t block_kth_largest(const uint32_t* keys, int n, int K, Smem& S,
-                                      int* rank_in_ties = nullptr) {
-  uint32_t prefix = 0;
-  int need = K;
-#pragma unroll 1
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    const uint32_t hmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
-    S.hist[threadIdx.x] = 0;  // NT == 256 bins
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += NT) {
-      const uint32_t k = keys[i];
-      if ((k & hmask) == prefix) atomicAdd(&S.hist[(k >> shift) & 255u], 1u);
-    }
-    __syncthreads();
-    // thread t owns digit 255 - t: exclusive scan of counts from the top digit down
-    const int d = 255 - (int)threadIdx.x;
-    const int cnt = (int)S.hist[d];
-    int tot;
-    const int above = block_excl_scan_i(cnt, &tot, S);
-    if (above < need && above + cnt >= need) {
-      S.sc[14] = d;
-      S.sc[15] = need - above;
-    }
-    __syncthreads();
-    prefix |= (uint32_t)S.sc[14] << shift;
-    need = S.sc[15];
-    __syncthreads();
-  }
-  if (rank_in_ties) *rank_in_ties = need;
-  return prefix;
-}
-
-// ascending bitonic sort of e[0, n), n a power of two
-__device__ void block_bitonic_sort(unsigned long long* e, int n) {
-  for (int k = 2; k <= n; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < n; i += NT) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const unsigned long long a = e[i], b = e[ixj];
-          const bool up = (i & k) == 0;
-          if ((a > b) == up) {
-            e[i] = b;
-            e[ixj] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------------------------
-// the segment pass: one CTA, one segment of one row -> one record
-// ---------------------------------------------------------------------------------------------
-template <typename TIn>
-__device__ void segment_pass(const KParams& P, const RowCfg& c, int row, int seg, Smem& S,
-                             unsigned char* rec) {
-  using E = Elem<TIn>;
-  constexpr int A = E::A;
-  constexpr int ES = 16 / A;
-  const int tid = threadIdx.x;
-  const int64_t lo = (int64_t)seg * P.seg_len;
-  const int64_t hi = min(P.V, lo + (int64_t)P.seg_len);
-  const int n = (int)(hi - lo);
-  const TIn* rowp = (const TIn*)P.logits + (int64_t)row * P.ld;
-  const int64_t gbase = P.voff + lo;  // global id of local index 0
-
-  // ---- 1. stage the segment in shared memory: 16-byte-aligned interior by TMA, edges by hand
-  const uintptr_t gaddr = (uintptr_t)(rowp + lo);
-  int head = (int)(((16u - (uint32_t)(gaddr & 15u)) & 15u) / ES);
-  if (head > n) head = n;
-  const int inter = (int)((((int64_t)(n - head) * ES) / 16) * 16 / ES);
-  const int tail0 = head + inter;
-  const int off = (A - head % A) % A;  // local index i lives at slot off + i
-  const int nvec = (off + n + A - 1) / A;
-  void* sv = S.sbuf;
-  if (tid == 0) {
-    mbar_init(&S.mbar, 1);
-  }
-  __syncthreads();
-  if (tid == 0 && inter > 0) {
-    const uint32_t bytes = (uint32_t)inter * ES;
-    mbar_expect_tx(&S.mbar, bytes);
-    for (uint32_t b = 0; b < bytes; b += 16384u) {
-      const uint32_t len = min(16384u, bytes - b);
-      tma_load_1d(S.sbuf + (size_t)(off + head) * ES + b,
-                  (const unsigned char*)(rowp + lo + head) + b, len, &S.mbar);
-    }
-  }
-  if (tid < off) E::neg_inf(sv, tid);
-  const int pad_end = nvec * A - (off + n);
-  if (tid < pad_end) E::neg_inf(sv, off + n + tid);
-  if (tid < head) E::copy(sv, off + tid, rowp, lo + tid);
-  if (tid < n - tail0) E::copy(sv, off + tail0 + tid, rowp, lo + tail0 + tid);
-  const int nwords = (nvec * A + 31) / 32;
-  for (int w = tid; w < nwords; w += NT) S.bitmap[w] = 0u;
-
-  // ---- 2. this segment's history entries (ids ascending within the row)
-  if (tid == 0) {
-    int64_t sa = 0, sb = 0;
-    if (c.pen) {
-      const int64_t a = P.hrow[row], b = P.hrow[row + 1];
-      sa = lower_bound_ids(P.hids, a, b, gbase);
-      sb = lower_bound_ids(P.hids, sa, b, gbase + n);
-    }
-    S.sc[0] = (int)(sb - sa);
-    S.sc[1] = (int)sa;
-    S.sc[2] = 0;  // candidate counter
-    S.sc[3] = 0;  // retained counter
-  }
-  // wait for the bulk copy (every thread observes the barrier phase itself)
-  bool ok = true;
-  if (inter > 0) ok = mbar_wait_bounded(&S.mbar, 0);
-  if (__syncthreads_or(!ok)) {
-    // the copy may still be in flight: wait once more, bounded, before touching anything
-    if (inter > 0) mbar_wait_bounded(&S.mbar, 0);
-    if (tid == 0) status_or(P, VINFER_ST_TIMEOUT);
-    RecHdr* h = (RecHdr*)rec;
-    if (tid == 0) { h->n = 0; h->flags = REC_OVERFLOW; h->t_key = 0; h->m_y = -INFINITY; h->s = 0.f; }
-    return;
-  }
-  const int ns_all = S.sc[0];
-  const int sbase = S.sc[1];
-  const bool side_over = ns_all > SIDE_CAP;
-  const int ns = side_over ? 0 : ns_all;
-  for (int j = tid; j < ns; j += NT) {
-    const int li = (int)((int64_t)__ldg(P.hids + sbase + j) - gbase);
-    const int cnt = __ldg(P.hcnt + sbase + j);
-    if (cnt > 0) {
-      const int slot = off + li;
-      S.side_li[j] = li;
-      S.side_y[j] = penalize(E::sm(sv, slot), cnt, c);
-      atomicOr(&S.bitmap[slot >> 5], 1u << (slot & 31));
-      E::neg_inf(sv, slot);
-    } else {
-      S.side_li[j] = -1;
-      S.side_y[j] = -INFINITY;
-    }
-  }
-  __syncthreads();
-
-  RecHdr* hdr = (RecHdr*)rec;
-  unsigned long long* ent = (unsigned long long*)(rec + sizeof(RecHdr));
-  if (side_over) {  // more penalised tokens than the side list holds: exact search
-    if (tid == 0) { hdr->n = 0; hdr->flags = REC_OVERFLOW; hdr->t_key = 0; hdr->m_y = -INFINITY; hdr->s = 0.f; }
-    return;
-  }
-
-  // ---- 3. one pass over shared memory: group maxima, online softmax sum, greedy argmax
-  const uint4* sv4 = (const uint4*)S.sbuf;
-  const int R = (nvec + NT - 1) / NT;
-  const int ngs = (R + GROUP_VECS - 1) / GROUP_VECS;
-  float m_t = -FLT_MAX, s_t = 0.f;
-  float best = -INFINITY;
-  int best_i = 0x7FFFFFFF;
-  float segmax = -INFINITY;
-  for (int g = 0; g < ngs; ++g) {
-    float gmx = -INFINITY;
-#pragma unroll
-    for (int rr = 0; rr < GROUP_VECS; ++rr) {
-      const int j = tid + (g * GROUP_VECS + rr) * NT;
-      if (j < nvec) {
-        const uint4 q = sv4[j];
-        const float vm = E::vmax(q);
-        gmx = fmaxf(gmx, vm);
-        if (c.need_sum) {
-          if (vm > m_t) {
-            s_t *= ex2((m_t - vm) * c.c2);
-            m_t = vm;
-          }
-#pragma unroll
-          for (int e = 0; e < A; ++e) s_t += ex2((E::at(q, e) - m_t) * c.c2);
-        }
-        if (c.greedy && vm > best) {
-          int e = 0;
-          while (e < A - 1 && E::at(q, e) != vm) ++e;
-          best = vm;
-          best_i = j * A + e - off;
-        }
-      }
-    }
-    S.gkey[g * NT + tid] = okey(gmx);
-    segmax = fmaxf(segmax, gmx);
-  }
-  // penalised tokens: singleton values in the side list, grouped by eight
-  const int nsg = (ns + SIDE_GROUP - 1) / SIDE_GROUP;
-  for (int sg = tid; sg < nsg; sg += NT) {
-    float gmx = -INFINITY;
-    for (int j = sg * SIDE_GROUP; j < min(ns, (sg + 1) * SIDE_GROUP); ++j) {
-      const float y = S.side_y[j];
-      gmx = fmaxf(gmx, y);
-      if (c.need_sum && S.side_li[j] >= 0) {
-        if (y > m_t) {
-          s_t *= ex2((m_t - y) * c.c2);
-          m_t = y;
-        }
-        s_t += ex2((y - m_t) * c.c2);
-      }
-      if (c.greedy && S.side_li[j] >= 0 &&
-          (y > best || (y == best && S.side_li[j] < best_i))) {
-        best = y;
-        best_i = S.side_li[j];
-      }
-    }
-    S.gkey[ngs * NT + sg] = okey(gmx);
-    segmax = fmaxf(segmax, gmx);
-  }
-  const uint32_t segmax_key = block_max_u32(okey(segmax), S);
-  const float m_seg = from_okey(segmax_key);
-
-  float s_seg = 0.f;
-  if (c.need_sum) {  // rescale every partial to the segment maximum, fixed order
-    const float part = (m_t == -FLT_MAX) ? 0.f : s_t * ex2((m_t - m_seg) * c.c2);
-    float tot;
-    block_excl_scan_f(part, &tot, S);
-    s_seg = tot;
-  }
-
-  if (c.greedy) {  // one entry: the first index of the maximum
-    const uint32_t k = okey(best);
-    const unsigned long long mine =
-        (best_i == 0x7FFFFFFF) ? ~0ull : comp(k, (int)(gbase + best_i));
-    const unsigned long long w = block_min_u64(mine, S);
-    if (tid == 0) {
-      hdr->m_y = m_seg;
-      hdr->s = 0.f;
-      hdr->t_key = 0;
-      hdr->flags = n > 1 ? REC_UNRETAINED : 0u;
-      hdr->n = (w == ~0ull) ? 0 : 1;
-      if (w != ~0ull) {
-        ent[0] = w;
-        hdr->t_key = comp_key(w);
-      }
-    }
-    return;
-  }
-
-  // ---- 4. threshold: the K-th largest group maximum bounds the K-th largest value from below
-  const int nkeys = ngs * NT + nsg;
-  uint32_t gk = 0;
-  if (c.K <= nkeys) gk = block_kth_largest(S.gkey, nkeys, c.K, S);
-  if (tid == 0) {
-    float ylo = -INFINITY;
-    if (gk > okey(-INFINITY)) {
-      const float g = from_okey(gk);
-      ylo = preimage_lo(vf(g, c), g, c);
-    }
-    S.sf[0] = ylo;
-  }
-  __syncthreads();
-  const float ylo = S.sf[0];
-  const uint32_t ylo_key = okey(ylo);
-
-  // ---- 5. rescan qualifying groups: every element with vf(y) >= vf(g) becomes a candidate
-  for (int g = 0; g < ngs; ++g) {
-    if (S.gkey[g * NT + tid] < ylo_key) continue;
-    for (int rr = 0; rr < GROUP_VECS; ++rr) {
-      const int j = tid + (g * GROUP_VECS + rr) * NT;
-      if (j >= nvec) break;
-      const uint4 q = sv4[j];
-#pragma unroll 1
-      for (int e = 0; e < A; ++e) {
-        const int slot = j * A + e;
-        const int li = slot - off;
-        if (li < 0 || li >= n) continue;
-        if (S.bitmap[slot >> 5] & (1u << (slot & 31))) continue;
-        const float y = E::at(q, e);
-        if (!(y >= ylo)) continue;
-        const int pos = atomicAdd(&S.sc[2], 1);
-        if (pos < CAND_CAP) {
-          S.ckey[pos] = okey(vf(y, c));
-          S.cid[pos] = (int)(gbase + li);
-        }
-      }
-    }
-  }
-  for (int sg = tid; sg < nsg; sg += NT) {
-    if (S.gkey[ngs * NT + sg] < ylo_key) continue;
-    for (int j = sg * SIDE_GROUP; j < min(ns, (sg + 1) * SIDE_GROUP); ++j) {
-      if (S.side_li[j] < 0 || !(S.side_y[j] >= ylo)) continue;
-      const int pos = atomicAdd(&S.sc[2], 1);
-      if (pos < CAND_CAP) {
-        S.ckey[pos] = okey(vf(S.side_y[j], c));
-        S.cid[pos] = (int)(gbase + S.side_li[j]);
-      }
-    }
-  }
-  __syncthreads();
-  const int nc_all = S.sc[2];
-  if (nc_all > CAND_CAP) {
-    if (tid == 0) { hdr->n = 0; hdr->flags = REC_OVERFLOW; hdr->t_key = 0; hdr->m_y = m_seg; hdr->s = s_seg; }
-    return;
-  }
-  const int nc = nc_all;
-
-  // ---- 6. exact K-th largest among candidates; keep everything at or above it (all ties)
-  uint32_t tk = 0;
-  if (nc >= c.K) tk = block_kth_largest(S.ckey, nc, c.K, S);
-  for (int i = tid; i < nc; i += NT) {
-    if (S.ckey[i] >= tk) {
-      const int pos = atomicAdd(&S.sc[3], 1);
-      ent[pos] = comp(S.ckey[i], S.cid[i]);
-    }
-  }
-  __syncthreads();
-  if (tid == 0) {
-    const int nr = S.sc[3];
-    hdr->m_y = m_seg;
-    hdr->s = s_seg;
-    hdr->n = nr;
-    hdr->t_key = tk;
-    hdr->flags = (nr < n) ? REC_UNRETAINED : 0u;
-  }
 }
 
 // ---------------------------------------------------------------------------------------------
 // merge: records -> canonical order -> cuts and draw
 // ---------------------------------------------------------------------------------------------
+__device__ void write_flag_hdr(RecHdr* h, uint32_t flags, float m_y, float s) {
+  h->m_y = m_y;
+  h->s = s;
+  h->t_key = 0;
+  h->n = 0;
+  h->flags = flags;
+}
+
 struct MergeIn {
   float m_y, s;
   uint32_t d_key;  // every element with key >= d_key is among the entries
@@ -759,57 +550,82 @@ struct MergeIn {
   int n;
 };
 
-// Gather the records of one row (nsrc sources at src0 + i * src_stride) into S.sbuf, sorted.
-__device__ MergeIn gather_records(const unsigned char* src0, size_t src_stride, int nsrc,
-                                  const RowCfg& c, Smem& S) {
-  unsigned long long* e = (unsigned long long*)S.sbuf;
-  int* offs = (int*)S.gkey;  // [nsrc + 1]
-  if (threadIdx.x == 0) {
+// number of entries of the ascending list e[0, n) below x
+__device__ __forceinline__ int lower_count(const unsigned long long* e, int n,
+                                           unsigned long long x) {
+  int a = 0, b = n;
+  while (a < b) {
+    const int mid = (a + b) >> 1;
+    if (e[mid] < x) a = mid + 1; else b = mid;
+  }
+  return a;
+}
+
+// Merge the sorted records of one row (nsrc sources at src0 + i * stride); the merged, sorted
+// entries land in out[0, MERGE_CAP) (the record entries are staged in the candidate buffer).
+__device__ MergeIn gather_sorted(const unsigned char* src0, size_t stride, int nsrc,
+                                 const RowCfg& c, Smem& S, unsigned long long* out) {
+  const int tid = threadIdx.x;
+  unsigned long long* in = S.cand;
+  if (tid < nsrc) {
+    const RecHdr* h = (const RecHdr*)(src0 + (size_t)tid * stride);
+    RecHdr r;
+    r.m_y = __ldcg(&h->m_y);
+    r.s = __ldcg(&h->s);
+    r.t_key = __ldcg(&h->t_key);
+    r.n = __ldcg(&h->n);
+    r.flags = __ldcg(&h->flags);
+    S.mh[tid] = r;
+  }
+  cbar();
+  if (tid == 0) {
     float m_y = -INFINITY;
-    for (int i = 0; i < nsrc; ++i) {
-      const RecHdr* h = (const RecHdr*)(src0 + (size_t)i * src_stride);
-      m_y = fmaxf(m_y, __ldcg(&h->m_y));
-    }
+    for (int i = 0; i < nsrc; ++i) m_y = fmaxf(m_y, S.mh[i].m_y);
     float s = 0.f;
     uint32_t d = 0, fl = 0;
     int tot = 0;
     for (int i = 0; i < nsrc; ++i) {
-      const RecHdr* h = (const RecHdr*)(src0 + (size_t)i * src_stride);
-      const uint32_t f = __ldcg(&h->flags);
-      const int n = __ldcg(&h->n);
-      const float hm = __ldcg(&h->m_y);
-      if (c.need_sum && hm > -INFINITY) s += __ldcg(&h->s) * ex2((hm - m_y) * c.c2);
-      if (f & REC_UNRETAINED) d = max(d, __ldcg(&h->t_key));
-      fl |= f;
-      offs[i] = tot;
-      tot += n;
+      const RecHdr& h = S.mh[i];
+      if (c.need_sum && h.m_y > -INFINITY) s += h.s * ex2((h.m_y - m_y) * c.c2);
+      if (h.flags & REC_UNRETAINED) d = max(d, h.t_key);
+      fl |= h.flags;
+      S.moff[i] = tot;
+      tot += h.n;
     }
-    offs[nsrc] = tot;
-    S.sf[1] = m_y;
-    S.sf[2] = s;
-    S.sc[4] = (int)d;
-    S.sc[5] = (int)fl;
-    S.sc[6] = tot;
+    S.moff[nsrc] = tot;
+    S.sf[SF_M] = m_y;
+    S.sf[SF_SK] = s;
+    S.sc[SC_X0] = (int)d;
+    S.sc[SC_X1] = (int)fl;
   }
-  __syncthreads();
+  cbar();
   MergeIn m;
-  m.m_y = S.sf[1];
-  m.s = S.sf[2];
-  m.d_key = (uint32_t)S.sc[4];
-  m.flags = (uint32_t)S.sc[5];
-  m.n = S.sc[6];
+  m.m_y = S.sf[SF_M];
+  m.s = S.sf[SF_SK];
+  m.d_key = (uint32_t)S.sc[SC_X0];
+  m.flags = (uint32_t)S.sc[SC_X1];
+  m.n = S.moff[nsrc];
   if ((m.flags & (REC_OVERFLOW | REC_BAD | REC_EXACT)) || m.n > MERGE_CAP) return m;
-  for (int i = 0; i < nsrc; ++i) {
-    const unsigned char* r = src0 + (size_t)i * src_stride;
-    const unsigned long long* re = (const unsigned long long*)(r + sizeof(RecHdr));
-    const int n = offs[i + 1] - offs[i];
-    for (int j = threadIdx.x; j < n; j += NT) e[offs[i] + j] = __ldcg(re + j);
+  for (int idx = tid; idx < m.n; idx += NT) {  // all sources at once: one round of loads
+    int s = 0;
+    while (S.moff[s + 1] <= idx) ++s;
+    const unsigned long long* re =
+        (const unsigned long long*)(src0 + (size_t)s * stride + sizeof(RecHdr));
+    in[idx] = __ldcg(re + (idx - S.moff[s]));
   }
-  int np = 1;
-  while (np < m.n) np <<= 1;
-  for (int j = m.n + threadIdx.x; j < np; j += NT) e[j] = ~0ull;
-  __syncthreads();
-  block_bitonic_sort(e, np);
+  cbar();
+  for (int idx = tid; idx < m.n; idx += NT) {
+    int s = 0;
+    while (S.moff[s + 1] <= idx) ++s;
+    const unsigned long long x = in[idx];
+    int rank = idx - S.moff[s];
+    for (int t = 0; t < nsrc; ++t) {
+      if (t == s) continue;
+      rank += lower_count(in + S.moff[t], S.moff[t + 1] - S.moff[t], x);
+    }
+    out[rank] = x;
+  }
+  cbar();
   return m;
 }
 
@@ -823,42 +639,40 @@ __device__ int count_ge(const unsigned long long* e, int n, uint32_t key) {
   return a;
 }
 
-// Finalize one row from sorted entries. Returns false when the row must take the exact search.
+__device__ void write_state(const KParams& P, int row, int kind, int token, float mv, float sk,
+                            uint32_t ck, int cid) {
+  P.out_ids[row] = token;
+  RowState st = {};
+  st.m_v = mv;
+  st.s_kept = sk;
+  st.cut_key = ck;
+  st.cut_id = cid;
+  st.kind = kind;
+  st.token = token;
+  P.rows[row] = st;
+}
+
+// Finalize one row from sorted entries e[0, m.n). Returns false when the row must take the
+// exact search.
 __device__ bool finalize_sorted(const KParams& P, const RowCfg& c, int row, const MergeIn& m,
-                                Smem& S) {
-  const unsigned long long* e = (const unsigned long long*)S.sbuf;
+                                const unsigned long long* e, Smem& S) {
   const int tid = threadIdx.x;
   if (m.n == 0) {
     if (tid == 0) {
-      P.out_ids[row] = -1;
+      write_state(P, row, 3, -1, 0.f, 0.f, 0u, 0);
       status_or(P, VINFER_ST_NONFINITE);
-      RowState st = {};
-      st.kind = 3;
-      st.token = -1;
-      P.rows[row] = st;
     }
     return true;
   }
   if (c.greedy) {
-    if (tid == 0) {
-      const int tok = comp_id(e[0]);
-      P.out_ids[row] = tok;
-      RowState st = {};
-      st.kind = 2;
-      st.token = tok;
-      P.rows[row] = st;
-    }
+    if (tid == 0) write_state(P, row, 2, comp_id(e[0]), 0.f, 0.f, 0u, 0);
     return true;
   }
   const float mv = from_okey(comp_key(e[0]));
   if (!(mv > -INFINITY) || !(mv <= FLT_MAX)) {
     if (tid == 0) {
-      P.out_ids[row] = -1;
+      write_state(P, row, 3, -1, 0.f, 0.f, 0u, 0);
       status_or(P, VINFER_ST_NONFINITE);
-      RowState st = {};
-      st.kind = 3;
-      st.token = -1;
-      P.rows[row] = st;
     }
     return true;
   }
@@ -877,7 +691,7 @@ __device__ bool finalize_sorted(const KParams& P, const RowCfg& c, int row, cons
   float loc = 0.f;
   for (int j = j0; j < j1; ++j) loc += ex2((from_okey(comp_key(e[j])) - mv) * LOG2E);
   float total;
-  const float pre = block_excl_scan_f(loc, &total, S);
+  const float pre = cta_excl_scan_f(loc, &total, S);
   const float Ssum = c.topk ? total : m.s;
   const bool listed_all = c.topk || !more;  // every kept-by-top-k token is among the entries
 
@@ -887,9 +701,12 @@ __device__ bool finalize_sorted(const KParams& P, const RowCfg& c, int row, cons
     float run = pre;
     for (int j = j0; j < min(j1, lim); ++j) {
       run += ex2((from_okey(comp_key(e[j])) - mv) * LOG2E);
-      if (ge ? (run >= t) : (run > t)) { hit = j; break; }
+      if (ge ? (run >= t) : (run > t)) {
+        hit = j;
+        break;
+      }
     }
-    return (int)block_min_u64((unsigned long long)(unsigned)hit, S);
+    return (int)cta_min_u64((unsigned long long)(unsigned)hit, S);
   };
 
   // L = length of the kept prefix: the smallest bound known to lie within the entries
@@ -905,8 +722,11 @@ __device__ bool finalize_sorted(const KParams& P, const RowCfg& c, int row, cons
   if (c.minp > 0.f) {  // min-p: keep tokens with exp(v - max) >= min_p
     int hit = 0x7FFFFFFF;
     for (int j = j0; j < j1; ++j)
-      if ((from_okey(comp_key(e[j])) - mv) * LOG2E < c.lm) { hit = j; break; }
-    hit = (int)block_min_u64((unsigned long long)(unsigned)hit, S);
+      if ((from_okey(comp_key(e[j])) - mv) * LOG2E < c.lm) {
+        hit = j;
+        break;
+      }
+    hit = (int)cta_min_u64((unsigned long long)(unsigned)hit, S);
     if (hit != 0x7FFFFFFF) L = min(L, max(hit, 1));
     else if (!listed_all) cut_beyond = true;
   }
@@ -915,40 +735,28 @@ __device__ bool finalize_sorted(const KParams& P, const RowCfg& c, int row, cons
   // kept-set mass
   float s_kept;
   if (L_known) {
-    if (tid == 0) S.sf[3] = 0.f;
-    __syncthreads();
     const int last = L - 1;
     if (last >= j0 && last < j1) {
       float run = pre;
       for (int j = j0; j <= last; ++j) run += ex2((from_okey(comp_key(e[j])) - mv) * LOG2E);
-      S.sf[3] = run;
+      S.sf[SF_SK] = run;
     }
-    __syncthreads();
-    s_kept = S.sf[3];
+    cbar();
+    s_kept = S.sf[SF_SK];
   } else {
     s_kept = Ssum;  // no cut at all: the kept set is every token
   }
-  const int lim = L_known ? min(L, avail) : avail;
+  const int lim = L_known ? L : avail;
   int j = first_cross(c.u * s_kept, false, lim);
   if (j == 0x7FFFFFFF) {
-    if (L_known && L <= avail) j = L - 1;
+    if (L_known) j = L - 1;
     else return false;
   }
   if (tid == 0) {
-    const int tok = comp_id(e[j]);
-    P.out_ids[row] = tok;
-    RowState st = {};
-    st.m_v = mv;
-    st.s_kept = s_kept;
-    st.token = tok;
-    if (L_known) {
-      st.kind = 0;
-      st.cut_key = comp_key(e[L - 1]);
-      st.cut_id = comp_id(e[L - 1]);
-    } else {
-      st.kind = 1;
-    }
-    P.rows[row] = st;
+    if (L_known)
+      write_state(P, row, 0, comp_id(e[j]), mv, s_kept, comp_key(e[L - 1]), comp_id(e[L - 1]));
+    else
+      write_state(P, row, 1, comp_id(e[j]), mv, s_kept, 0u, 0);
   }
   return true;
 }
@@ -956,24 +764,28 @@ __device__ bool finalize_sorted(const KParams& P, const RowCfg& c, int row, cons
 // ---------------------------------------------------------------------------------------------
 // exact multi-pass search over one row (global memory), for rows the records cannot resolve
 // ---------------------------------------------------------------------------------------------
+// penalised-position bitmap of a whole row: the candidate buffer's words first, then a stage's
+struct RowBits {
+  uint32_t* w0;
+  uint32_t* w1;
+  static constexpr int N0 = RUN_CAP * 2;
+  __device__ uint32_t& word(int w) const { return w < N0 ? w0[w] : w1[w - N0]; }
+  __device__ bool bit(int i) const { return (word(i >> 5) >> (i & 31)) & 1u; }
+};
+
 template <typename TIn>
 struct ExactRow {
   const KParams& P;
   const RowCfg& c;
-  Smem& S;
+  RowBits bm;  // penalised positions of the row
   const TIn* rowp;
   int64_t hist_a, hist_b;
   int V;
   float mv;
-  uint32_t tk;  // kept by top-k: key >= tk
 
-  __device__ bool pen_bit(int i) const {
-    const uint32_t* bm = (const uint32_t*)S.sbuf;
-    return (bm[i >> 5] >> (i & 31)) & 1u;
-  }
   __device__ float y_at(int i) const {
     float x = Elem<TIn>::ld(rowp, i);
-    if (c.pen && pen_bit(i)) {
+    if (c.pen && bm.bit(i)) {
       const int64_t p = lower_bound_ids(P.hids, hist_a, hist_b, P.voff + i);
       x = penalize(x, __ldg(P.hcnt + p), c);
     }
@@ -986,13 +798,37 @@ struct ExactRow {
   }
 };
 
+// Histogram update for one element per lane (`ok` lanes only). When every active lane of the
+// warp falls in the same bin, which is the common case on the coarse levels of a float radix,
+// the warp adds its totals once instead of contending 32 times on one address.
+__device__ __forceinline__ void warp_bin_add(bool ok, uint32_t b, unsigned long long mw,
+                                             uint32_t* cnt, unsigned long long* mass) {
+  const unsigned act = __ballot_sync(FULLMASK, ok);
+  if (!act) return;
+  const int lane = threadIdx.x & 31;
+  const int ldr = __ffs(act) - 1;
+  const uint32_t bl = __shfl_sync(FULLMASK, b, ldr);
+  if (__all_sync(FULLMASK, !ok || b == bl)) {
+    unsigned long long sum = mw;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(FULLMASK, sum, o);
+    if (lane == ldr) {
+      atomicAdd(&cnt[bl], (uint32_t)__popc(act));
+      if (mass) atomicAdd(&mass[bl], sum);
+    }
+  } else if (ok) {
+    atomicAdd(&cnt[b], 1u);
+    if (mass) atomicAdd(&mass[b], mw);
+  }
+}
+
 // kept-set predicate of the exact search
 struct Cut {
-  uint32_t tk;       // top-k: key >= tk
-  int kind;          // 0: (key > ck) or (key == ck and i <= cid); 1: all
+  uint32_t tk;  // top-k: key >= tk
+  int kind;     // 0: (key > ck) or (key == ck and i <= cid); 1: all
   uint32_t ck;
   int cid;
-  uint32_t mk;       // min-p: key >= mk
+  uint32_t mk;  // min-p: key >= mk
   __device__ bool keep(uint32_t key, int i) const {
     if (key < tk || key < mk) return false;
     if (kind == 1) return true;
@@ -1001,84 +837,70 @@ struct Cut {
 };
 
 struct Found {
-  uint32_t w;                 // key of the tie group reached
-  unsigned long long above;   // fixed-point mass strictly above w (kept elements)
-  int j;                      // 1-based rank inside the tie group, ascending id
+  uint32_t w;                // key of the tie group reached
+  unsigned long long above;  // fixed-point mass strictly above w (kept elements)
+  int j;                     // 1-based rank inside the tie group, ascending id
   int n_w;
 };
 
+// Canonical position where the cumulative kept mass first reaches (>=) or passes (>) target:
+// four levels of 8-bit radix histograms of count and fixed-point mass over the keys.
 template <typename TIn>
-__device__ Found exact_search(ExactRow<TIn>& X, const Cut& cut, unsigned long long target,
-                              bool strict) {
-  Smem& S = X.S;
-  static_assert(FB_BINS * 4 <= sizeof(Smem::ckey) + sizeof(Smem::cid), "count bins fit");
-  static_assert(FB_BINS * 8 <= sizeof(Smem::side_li) + sizeof(Smem::side_y), "mass bins fit");
-  uint32_t* cnt = (uint32_t*)S.ckey;                // FB_BINS counts (ckey + cid region)
-  unsigned long long* mass = (unsigned long long*)S.side_li;  // FB_BINS masses
+__device__ Found exact_search(const ExactRow<TIn>& X, const Cut& cut, unsigned long long target,
+                              bool strict, Smem& S) {
+  uint32_t* cnt = S.bin_cnt;
+  unsigned long long* mass = S.bin_mass;
+  const int tid = threadIdx.x;
   uint32_t prefix = 0;
   unsigned long long above = 0;
   int last_cnt = 0;
-  const int shifts[3] = {21, 10, 0};
-  const int bitsv[3] = {11, 11, 10};
 #pragma unroll 1
-  for (int lv = 0; lv < 3; ++lv) {
-    const int sh = shifts[lv], nb = 1 << bitsv[lv];
-    for (int b = threadIdx.x; b < nb; b += NT) { cnt[b] = 0; mass[b] = 0ull; }
-    __syncthreads();
-    for (int i = threadIdx.x; i < X.V; i += NT) {
-      const uint32_t key = X.key_at(i);
-      if (!cut.keep(key, i)) continue;
-      if (lv > 0 && (key >> (sh + bitsv[lv])) != prefix) continue;
-      const uint32_t b = (key >> sh) & (uint32_t)(nb - 1);
-      atomicAdd(&cnt[b], 1u);
-      atomicAdd(&mass[b], X.wfx(key));
+  for (int lv = 0; lv < 4; ++lv) {
+    const int sh = 24 - 8 * lv;
+    cnt[tid] = 0;
+    mass[tid] = 0ull;
+    cbar();
+    for (int base = 0; base < X.V; base += NT) {
+      const int i = base + tid;
+      bool ok = i < X.V;
+      uint32_t key = 0;
+      if (ok) {
+        key = X.key_at(i);
+        ok = cut.keep(key, i) && (lv == 0 || (key >> (sh + 8)) == prefix);
+      }
+      warp_bin_add(ok, (key >> sh) & 255u, ok ? X.wfx(key) : 0ull, cnt, mass);
     }
-    __syncthreads();
-    // bins in descending order; thread t owns nb / NT consecutive ones
-    const int per = nb / NT;
-    const int b_hi = nb - 1 - threadIdx.x * per;
-    unsigned long long mine = 0;
-    for (int q = 0; q < per; ++q) mine += mass[b_hi - q];
+    cbar();
+    // thread t owns bin 255 - t, so thread order is descending key order
+    const int b = 255 - tid;
+    const unsigned long long mb = mass[b];
+    const uint32_t cb = cnt[b];
     unsigned long long tot;
-    const unsigned long long ex = block_excl_scan_u64(mine, &tot, S);
-    unsigned long long hit = ~0ull;
-    {
-      unsigned long long run = above + ex;
-      for (int q = 0; q < per; ++q) {
-        const int b = b_hi - q;
-        if (cnt[b] == 0) continue;
-        const unsigned long long nxt = run + mass[b];
-        if (strict ? (nxt > target) : (nxt >= target)) {
-          hit = ((unsigned long long)(threadIdx.x * per + q) << 32) | (unsigned)b;
-          break;
-        }
-        run = nxt;
-      }
-    }
-    hit = block_min_u64(hit, S);
-    if (hit == ~0ull) {
-      // target at or beyond the total (rounding): take the lowest non-empty bin
-      unsigned long long lowb = ~0ull;
-      for (int q = 0; q < per; ++q) {
-        const int b = b_hi - q;
-        if (cnt[b]) lowb = ((unsigned long long)(NT * per - (threadIdx.x * per + q)) << 32) | (unsigned)b;
-      }
-      hit = block_min_u64(lowb, S);
-      if (hit == ~0ull) {  // nothing kept at all
-        Found f = {0, 0, 0, 0};
+    const unsigned long long ex = cta_excl_scan_u64(mb, &tot, S);
+    const unsigned long long before = above + ex, after = before + mb;
+    const bool cross_after = strict ? (after > target) : (after >= target);
+    const bool cross_before = strict ? (before > target) : (before >= target);
+    unsigned long long pick = ~0ull;
+    if (cb > 0 && cross_after && !cross_before) pick = (unsigned long long)tid;
+    pick = cta_min_u64(pick, S);
+    if (pick == ~0ull) {  // target at or beyond the total (rounding): the lowest non-empty bin
+      pick = cta_min_u64(cb > 0 ? (unsigned long long)(NT - 1 - tid) : ~0ull, S);
+      if (pick == ~0ull) {
+        Found f = {0u, 0ull, 0, 0};
         return f;
       }
+      pick = (unsigned long long)(NT - 1 - (int)pick);
     }
-    const int b = (int)(uint32_t)hit;
-    // mass strictly above bin b at this level
-    unsigned long long part = 0;
-    for (int q = 0; q < per; ++q)
-      if (b_hi - q > b) part += mass[b_hi - q];
-    const unsigned long long ab = block_sum_u64(part, S);
-    above += ab;
-    prefix = (prefix << bitsv[lv]) | (uint32_t)b;
-    last_cnt = (int)cnt[b];
-    __syncthreads();
+    if ((int)pick == tid) {
+      S.sc[SC_B] = b;
+      S.red64[NCW] = before;
+      S.sc[SC_J] = (int)cb;
+    }
+    cbar();
+    prefix = (prefix << 8) | (uint32_t)S.sc[SC_B];
+    above = S.red64[NCW];
+    last_cnt = S.sc[SC_J];
+    cbar();
   }
   Found f;
   f.w = prefix;
@@ -1088,9 +910,8 @@ __device__ Found exact_search(ExactRow<TIn>& X, const Cut& cut, unsigned long lo
   long long j;
   if (ew == 0) {
     j = last_cnt;
-  } else if (target <= above) {
-    j = strict ? 1 : 1;
-    if (strict && target >= above) j = (long long)((target - above) / ew) + 1;
+  } else if (target < above) {
+    j = 1;
   } else {
     const unsigned long long d = target - above;
     j = strict ? (long long)(d / ew) + 1 : (long long)((d + ew - 1) / ew);
@@ -1103,8 +924,7 @@ __device__ Found exact_search(ExactRow<TIn>& X, const Cut& cut, unsigned long lo
 
 // index of the j-th (1-based) kept element with key == w, in ascending index order
 template <typename TIn>
-__device__ int exact_jth(ExactRow<TIn>& X, const Cut& cut, uint32_t w, int j) {
-  Smem& S = X.S;
+__device__ int exact_jth(const ExactRow<TIn>& X, const Cut& cut, uint32_t w, int j, Smem& S) {
   constexpr int PER = 8;
   for (int base = 0; base < X.V; base += NT * PER) {
     const int i0 = base + threadIdx.x * PER;
@@ -1114,125 +934,120 @@ __device__ int exact_jth(ExactRow<TIn>& X, const Cut& cut, uint32_t w, int j) {
       if (key == w && cut.keep(key, i)) ++cntm;
     }
     int tot;
-    const int ex = block_excl_scan_i(cntm, &tot, S);
+    const int ex = cta_excl_scan_i(cntm, &tot, S);
     if (j <= tot) {
       if (ex < j && j <= ex + cntm) {
         int r = j - ex;
         for (int i = i0; i < min(i0 + PER, X.V); ++i) {
           const uint32_t key = X.key_at(i);
-          if (key == w && cut.keep(key, i) && --r == 0) { S.sc[7] = i; break; }
+          if (key == w && cut.keep(key, i) && --r == 0) {
+            S.sc[SC_J] = i;
+            break;
+          }
         }
       }
-      __syncthreads();
-      return S.sc[7];
+      cbar();
+      return S.sc[SC_J];
     }
     j -= tot;
-    __syncthreads();
   }
   return -1;
 }
 
 template <typename TIn>
-__device__ void exact_row(const KParams& P, const RowCfg& c, int row, Smem& S) {
+__device__ void exact_row(const KParams& P, const RowCfg& c, int row, Smem& S,
+                          unsigned char* scratch) {
   const int tid = threadIdx.x;
-  ExactRow<TIn> X{P, c, S, (const TIn*)P.logits + (int64_t)row * P.ld, 0, 0, (int)P.V,
-                  0.f, 0u};
-  // penalised-position bitmap of the whole row
-  uint32_t* bm = (uint32_t*)S.sbuf;
+  const RowBits bm{(uint32_t*)S.cand, (uint32_t*)scratch};
+  ExactRow<TIn> X{P, c, bm, (const TIn*)P.logits + (int64_t)row * P.ld, 0, 0, (int)P.V, 0.f};
   const int words = (X.V + 31) / 32;
-  for (int w = tid; w < words; w += NT) bm[w] = 0u;
-  __syncthreads();
+  for (int w = tid; w < words; w += NT) bm.word(w) = 0u;
+  cbar();
   if (c.pen) {
     const int64_t a = P.hrow[row], b = P.hrow[row + 1];
-    const int64_t sa = lower_bound_ids(P.hids, a, b, P.voff);
-    const int64_t sb = lower_bound_ids(P.hids, sa, b, P.voff + X.V);
-    X.hist_a = sa;
-    X.hist_b = sb;
-    for (int64_t q = sa + tid; q < sb; q += NT) {
+    X.hist_a = lower_bound_ids(P.hids, a, b, P.voff);
+    X.hist_b = lower_bound_ids(P.hids, X.hist_a, b, P.voff + X.V);
+    for (int64_t q = X.hist_a + tid; q < X.hist_b; q += NT) {
       if (__ldg(P.hcnt + q) > 0) {
         const int i = (int)(__ldg(P.hids + q) - P.voff);
-        atomicOr(&bm[i >> 5], 1u << (i & 31));
+        atomicOr(&bm.word(i >> 5), 1u << (i & 31));
       }
     }
   }
-  __syncthreads();
+  cbar();
   // maximum (and, for greedy rows, the first index of it)
   unsigned long long best = ~0ull;
   for (int i = tid; i < X.V; i += NT) {
     const unsigned long long cc = comp(X.key_at(i), (int)(P.voff + i));
     best = cc < best ? cc : best;
   }
-  best = block_min_u64(best, S);
-  const uint32_t mkey = comp_key(best);
-  X.mv = from_okey(mkey);
+  best = cta_min_u64(best, S);
+  X.mv = from_okey(comp_key(best));
   if (c.greedy) {
-    if (tid == 0) {
-      P.out_ids[row] = comp_id(best);
-      RowState st = {};
-      st.kind = 2;
-      st.token = comp_id(best);
-      P.rows[row] = st;
-    }
+    if (tid == 0) write_state(P, row, 2, comp_id(best), 0.f, 0.f, 0u, 0);
     return;
   }
   if (!(X.mv > -INFINITY) || !(X.mv <= FLT_MAX)) {
     if (tid == 0) {
-      P.out_ids[row] = -1;
+      write_state(P, row, 3, -1, 0.f, 0.f, 0u, 0);
       status_or(P, VINFER_ST_NONFINITE);
-      RowState st = {};
-      st.kind = 3;
-      st.token = -1;
-      P.rows[row] = st;
     }
     return;
   }
   // top-k threshold: radix select over the keys of the whole row (8-bit digits)
   uint32_t tk = 0;
   if (c.topk) {
+    uint32_t* hist = S.bin_cnt;
     uint32_t prefix = 0;
     int need = c.k;
 #pragma unroll 1
     for (int pass = 0; pass < 4; ++pass) {
       const int shift = 24 - 8 * pass;
       const uint32_t hmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
-      S.hist[tid] = 0;
-      __syncthreads();
-      for (int i = tid; i < X.V; i += NT) {
-        const uint32_t k = X.key_at(i);
-        if ((k & hmask) == prefix) atomicAdd(&S.hist[(k >> shift) & 255u], 1u);
+      hist[tid] = 0;
+      cbar();
+      for (int base = 0; base < X.V; base += NT) {
+        const int i = base + tid;
+        bool ok = i < X.V;
+        uint32_t k = 0;
+        if (ok) {
+          k = X.key_at(i);
+          ok = (k & hmask) == prefix;
+        }
+        warp_bin_add(ok, (k >> shift) & 255u, 0ull, hist, nullptr);
       }
-      __syncthreads();
+      cbar();
       const int d = 255 - tid;
-      const int cnt = (int)S.hist[d];
+      const int cnt = (int)hist[d];
       int tot;
-      const int above = block_excl_scan_i(cnt, &tot, S);
+      const int above = cta_excl_scan_i(cnt, &tot, S);
       if (above < need && above + cnt >= need) {
-        S.sc[14] = d;
-        S.sc[15] = need - above;
+        S.sc[SC_B] = d;
+        S.sc[SC_J] = need - above;
       }
-      __syncthreads();
-      prefix |= (uint32_t)S.sc[14] << shift;
-      need = S.sc[15];
-      __syncthreads();
+      cbar();
+      prefix |= (uint32_t)S.sc[SC_B] << shift;
+      need = S.sc[SC_J];
+      cbar();
     }
     tk = prefix;
   }
-  Cut base = {tk, 1, 0u, 0, 0u};
+  const Cut base = {tk, 1, 0u, 0, 0u};
   // total mass of the kept-by-top-k set, fixed point
   unsigned long long part = 0;
   for (int i = tid; i < X.V; i += NT) {
     const uint32_t key = X.key_at(i);
     if (base.keep(key, i)) part += X.wfx(key);
   }
-  const unsigned long long S_fx = block_sum_u64(part, S);
+  const unsigned long long S_fx = cta_sum_u64(part, S);
   Cut fin = base;
   unsigned long long s_kept = S_fx;
   bool cut_set = false;
   if (c.p < 1.f) {
     const unsigned long long tgt = (unsigned long long)((double)c.p * (double)S_fx);
-    const Found f = exact_search(X, base, tgt, false);
+    const Found f = exact_search(X, base, tgt, false, S);
     if (f.n_w > 0) {
-      const int id = exact_jth(X, base, f.w, f.j);
+      const int id = exact_jth(X, base, f.w, f.j, S);
       fin.kind = 0;
       fin.ck = f.w;
       fin.cid = id;
@@ -1241,10 +1056,9 @@ __device__ void exact_row(const KParams& P, const RowCfg& c, int row, Smem& S) {
     }
   }
   if (c.minp > 0.f) {
-    // smallest key passing min-p: keys are monotone in v, test by value
+    // min-p keeps a prefix by value; it binds when the top-p cut lies below its threshold
     const bool binds = !cut_set || ((from_okey(fin.ck) - X.mv) * LOG2E < c.lm);
     if (binds) {
-      Cut mc = base;
       unsigned long long pm = 0;
       uint32_t kmin = 0xFFFFFFFFu;
       for (int i = tid; i < X.V; i += NT) {
@@ -1254,99 +1068,47 @@ __device__ void exact_row(const KParams& P, const RowCfg& c, int row, Smem& S) {
         pm += X.wfx(key);
         kmin = min(kmin, key);
       }
-      const unsigned long long pms = block_sum_u64(pm, S);
-      const uint32_t km = (uint32_t)(~block_max_u32(~kmin, S));
-      mc.mk = km;
-      fin = mc;
+      const unsigned long long pms = cta_sum_u64(pm, S);
+      const uint32_t km = ~cta_max_u32(~kmin, S);
+      fin = base;
+      fin.mk = km;
       s_kept = pms;
-      cut_set = true;
     }
   }
   const unsigned long long tgt = (unsigned long long)((double)c.u * (double)s_kept);
-  const Found fd = exact_search(X, fin, tgt, true);
+  const Found fd = exact_search(X, fin, tgt, true, S);
   int tok = -1;
-  if (fd.n_w > 0) tok = exact_jth(X, fin, fd.w, fd.j);
+  if (fd.n_w > 0) tok = exact_jth(X, fin, fd.w, fd.j, S);
   if (tid == 0) {
     if (tok < 0) status_or(P, VINFER_ST_INTERNAL);
-    P.out_ids[row] = tok < 0 ? -1 : (int)(P.voff + tok);
-    RowState st = {};
-    st.m_v = X.mv;
-    st.s_kept = (float)((double)s_kept / FX_ONE);
-    st.token = P.out_ids[row];
-    if (fin.kind == 0) {
-      st.kind = 0;
-      st.cut_key = fin.ck;
-      st.cut_id = (int)(P.voff + fin.cid);
-    } else if (fin.mk != 0u) {
-      st.kind = 0;
-      st.cut_key = fin.mk;
-      st.cut_id = 0x7FFFFFFF;
-    } else if (c.topk) {
-      st.kind = 0;
-      st.cut_key = tk;
-      st.cut_id = 0x7FFFFFFF;
-    } else {
-      st.kind = 1;
-    }
-    P.rows[row] = st;
+    const int gtok = tok < 0 ? -1 : (int)(P.voff + tok);
+    const float sk = (float)((double)s_kept / FX_ONE);
+    if (fin.kind == 0) write_state(P, row, 0, gtok, X.mv, sk, fin.ck, (int)(P.voff + fin.cid));
+    else if (fin.mk != 0u) write_state(P, row, 0, gtok, X.mv, sk, fin.mk, 0x7FFFFFFF);
+    else if (c.topk) write_state(P, row, 0, gtok, X.mv, sk, tk, 0x7FFFFFFF);
+    else write_state(P, row, 1, gtok, X.mv, sk, 0u, 0);
   }
 }
 
 // ---------------------------------------------------------------------------------------------
-// kernels
+// finishing a row: local shard record, final answer, or the exact search
 // ---------------------------------------------------------------------------------------------
 template <typename TIn>
-__global__ void __launch_bounds__(NT, 3) k_sample(const KParams P) {
-  extern __shared__ __align__(128) unsigned char smraw[];
-  Smem& S = *reinterpret_cast<Smem*>(smraw);
-  const int seg = blockIdx.x, row = blockIdx.y, tid = threadIdx.x;
+__device__ void finish_row(const KParams& P, Smem& S, unsigned char* scratch, int row,
+                           const unsigned char* src0, size_t stride, int nsrc, bool local,
+                           int* unresolved) {
+  const int tid = threadIdx.x;
   const RowCfg c = load_row(P, row);
-  unsigned char* rec = P.recs + ((size_t)row * P.nseg + seg) * REC_STRIDE;
-  const bool local = P.mode == 1;
-  if (c.bad || c.exact) {
-    if (tid == 0) {
-      RecHdr* h = (RecHdr*)rec;
-      h->n = 0;
-      h->flags = c.bad ? REC_BAD : REC_EXACT;
-      h->t_key = 0;
-      h->m_y = -INFINITY;
-      h->s = 0.f;
-    }
-  } else {
-    segment_pass<TIn>(P, c, row, seg, S, rec);
-  }
-  // completion count: the last CTA of the row merges
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int old = atomicAdd(&P.counters[row], 1);
-    const int last = (old == P.nseg - 1);
-    if (last) {
-      __threadfence();
-      P.counters[row] = 0;  // ready for the next call
-    }
-    S.sc[8] = last;
-  }
-  __syncthreads();
-  if (!S.sc[8]) return;
-  __threadfence();
-
-  const MergeIn m = gather_records(P.recs + (size_t)row * P.nseg * REC_STRIDE, REC_STRIDE,
-                                   P.nseg, c, S);
+  const MergeIn m = gather_sorted(src0, stride, nsrc, c, S, (unsigned long long*)scratch);
+  const unsigned long long* e = (const unsigned long long*)scratch;
   if (local) {
-    // write this rank's shard record: entries at or above the K-th, all ties, <= shard_cap
+    // this rank's shard record: entries at or above the K-th, all ties, <= shard_cap
     unsigned char* out = P.shard_out + (size_t)row * P.shard_stride;
     RecHdr* oh = (RecHdr*)out;
     unsigned long long* oe = (unsigned long long*)(out + sizeof(RecHdr));
-    const unsigned long long* e = (const unsigned long long*)S.sbuf;
     if ((m.flags & (REC_OVERFLOW | REC_BAD | REC_EXACT)) || m.n > MERGE_CAP) {
-      if (tid == 0) {
-        oh->n = 0;
-        oh->flags = (m.flags & REC_BAD) ? REC_BAD : REC_OVERFLOW;
-        oh->t_key = 0;
-        oh->m_y = m.m_y;
-        oh->s = m.s;
-      }
+      if (tid == 0)
+        write_flag_hdr(oh, (m.flags & REC_BAD) ? REC_BAD : REC_OVERFLOW, m.m_y, m.s);
       return;
     }
     int nr = m.n;
@@ -1356,75 +1118,613 @@ __global__ void __launch_bounds__(NT, 3) k_sample(const KParams P) {
       nr = count_ge(e, m.n, tkey);
     }
     const bool over = nr > P.shard_cap;
+    const bool unret = (m.flags & REC_UNRETAINED) || nr < m.n;
     for (int j = tid; j < min(nr, P.shard_cap); j += NT) oe[j] = e[j];
     if (tid == 0) {
       oh->m_y = m.m_y;
       oh->s = m.s;
       oh->n = over ? 0 : nr;
-      oh->t_key = (m.flags & REC_UNRETAINED) || nr < m.n ? max(tkey, m.d_key) : 0u;
-      oh->flags = over ? REC_OVERFLOW
-                       : (((m.flags & REC_UNRETAINED) || nr < m.n) ? REC_UNRETAINED : 0u);
+      oh->t_key = unret ? max(tkey, m.d_key) : 0u;
+      oh->flags = over ? REC_OVERFLOW : (unret ? REC_UNRETAINED : 0u);
     }
     return;
   }
   if (m.flags & REC_BAD) {
     if (tid == 0) {
-      P.out_ids[row] = -1;
+      write_state(P, row, 3, -1, 0.f, 0.f, 0u, 0);
       status_or(P, VINFER_ST_BAD_PARAM);
-      RowState st = {};
-      st.kind = 3;
-      st.token = -1;
-      P.rows[row] = st;
+      if (unresolved) unresolved[row] = 0;
     }
     return;
   }
   bool done = false;
-  if (!(m.flags & (REC_OVERFLOW | REC_EXACT)) && m.n <= MERGE_CAP) {
-    done = finalize_sorted(P, c, row, m, S);
+  if (!(m.flags & (REC_OVERFLOW | REC_EXACT)) && m.n <= MERGE_CAP)
+    done = finalize_sorted(P, c, row, m, e, S);
+  if (unresolved) {  // sharded merge: the caller resolves the row from the full logits
+    if (tid == 0) {
+      unresolved[row] = done ? 0 : 1;
+      if (!done) write_state(P, row, 3, -1, 0.f, 0.f, 0u, 0);
+    }
+    return;
   }
-  __syncthreads();
-  if (!done) exact_row<TIn>(P, c, row, S);
+  cbar();
+  if (!done) exact_row<TIn>(P, c, row, S, scratch);
 }
 
-// merge of gathered shard records: one CTA per row
-__global__ void __launch_bounds__(NT) k_merge(const KParams P, const unsigned char* recs,
+// ---------------------------------------------------------------------------------------------
+// work decomposition: CTA b owns segments [seg_begin(b), seg_begin(b + 1)) of the row-major list
+// of B * nseg segments; a run is its maximal part inside one row
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ int seg_begin(const KParams& P, int b) {
+  return (int)(((int64_t)b * P.total) / P.grid);
+}
+__device__ __forceinline__ int seg_owner(const KParams& P, int sg) {
+  return (int)((((int64_t)sg + 1) * P.grid - 1) / P.total);
+}
+
+// ---------------------------------------------------------------------------------------------
+// producer warp: stages segments for the consumers
+// ---------------------------------------------------------------------------------------------
+template <typename TIn>
+__device__ void producer(const KParams& P, Smem& S) {
+  using E = Elem<TIn>;
+  constexpr int ES = 16 / E::A;
+  const int lane = threadIdx.x & 31;
+  const int s0 = seg_begin(P, blockIdx.x), s1 = seg_begin(P, blockIdx.x + 1);
+  float prm = 0.f;
+  bool pen = false;
+  int64_t hp = 0, hend = 0;
+  for (int i = 0; s0 + i < s1; ++i) {
+    const int sg = s0 + i, row = sg / P.nseg, seg = sg - row * P.nseg;
+    const int s = i % NSTAGE, use = i / NSTAGE;
+    const Geo g = geometry<TIn>(P, row, seg);
+    if (i == 0 || seg == 0) {  // a new run: the row's parameters and history position
+      prm = lane < 8 ? load_param(P, row, lane) : 0.f;
+      const float rep = __shfl_sync(FULLMASK, prm, 3);
+      const float pres = __shfl_sync(FULLMASK, prm, 4);
+      const float freq = __shfl_sync(FULLMASK, prm, 5);
+      pen = P.hrow != nullptr && (rep != 1.f || pres != 0.f || freq != 0.f);
+      if (pen) {
+        const int64_t a = __ldg(P.hrow + row);
+        hend = __ldg(P.hrow + row + 1);
+        hp = seg == 0 ? a : warp_lower_bound(P.hids, a, hend, g.gbase, lane);
+      }
+    }
+    // penalised tokens of this segment: the next entries of the row's ascending history
+    int ns = 0;
+    int rid[SIDE_PER_LANE], rcn[SIDE_PER_LANE];
+    if (pen) {
+      const int64_t lim = g.gbase + g.n;
+#pragma unroll
+      for (int q = 0; q < SIDE_PER_LANE; ++q) {
+        const int64_t p = hp + lane + 32 * q;
+        rid[q] = p < hend ? __ldg(P.hids + p) : 0x7FFFFFFF;
+        rcn[q] = p < hend ? __ldg(P.hcnt + p) : 0;
+      }
+#pragma unroll
+      for (int q = 0; q < SIDE_PER_LANE; ++q)
+        ns += __popc(__ballot_sync(FULLMASK, (int64_t)rid[q] < lim));
+      if (ns == SIDE_CAP) {  // the window is full: find the end of this segment's entries
+        const int64_t e = warp_lower_bound(P.hids, hp + SIDE_CAP, hend, lim, lane);
+        if (e > hp + SIDE_CAP) {
+          hp = e;
+          ns = -1;  // more penalised tokens than a stage holds: the row takes the exact search
+        } else {
+          hp += SIDE_CAP;
+        }
+      } else {
+        hp += ns;
+      }
+    }
+    uint32_t hv = 0, tv = 0;
+    if (lane < g.head) hv = E::ldraw(g.rowp, g.lo + lane);
+    if (lane < g.n - g.tail0) tv = E::ldraw(g.rowp, g.lo + g.tail0 + lane);
+    // ---- wait until the consumers released this stage's previous segment
+    if (use >= 1 && !mbar_wait_bounded(&S.empty[s], (use - 1) & 1)) {
+      if (lane == 0) status_or(P, VINFER_ST_TIMEOUT);
+      return;
+    }
+    Stage& st = S.st[s];
+    if (lane < 8) st.prm[lane] = prm;
+    if (lane == 0) st.ns = ns;
+#pragma unroll
+    for (int q = 0; q < SIDE_PER_LANE; ++q) {
+      const int j = lane + 32 * q;
+      if (j < ns) {
+        st.side_id[j] = rid[q];
+        st.side_cnt[j] = rcn[q];
+      }
+    }
+    if (lane < g.off) E::neg_inf(st.data, lane);
+    if (lane < g.pad_end) E::neg_inf(st.data, g.off + g.n + lane);
+    if (lane < g.head) E::straw(st.data, g.off + lane, hv);
+    if (lane < g.n - g.tail0) E::straw(st.data, g.off + g.tail0 + lane, tv);
+    __syncwarp();
+    if (lane == 0) {
+      const uint32_t bytes = (uint32_t)g.inter * ES;
+      mbar_arrive_expect_tx(&S.full[s], bytes);
+      for (uint32_t b = 0; b < bytes; b += 16384u) {
+        tma_load_1d(st.data + (size_t)(g.off + g.head) * ES + b,
+                    (const unsigned char*)((const TIn*)g.rowp + g.lo + g.head) + b,
+                    min(16384u, bytes - b), &S.full[s]);
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// consumers
+// ---------------------------------------------------------------------------------------------
+// smallest y with vf(y) >= vt: about y = vt * T; the boundary lies within a few keys of it in
+// the normal range, found by one round of 32 probes (a full binary search otherwise)
+__device__ float ylo_for(float vt, const RowCfg& c) {
+  if (c.greedy || vt == -INFINITY) return vt;
+  const int lane = threadIdx.x & 31;
+  const uint32_t k0 = okey(vt * c.T);
+  const bool inside = k0 > okey(-INFINITY) + 16u && k0 < okey(INFINITY) - 16u;
+  const uint32_t kp = inside ? k0 - 16u + (uint32_t)lane : k0;  // probes k0 - 16 .. k0 + 15
+  const bool ge = vf(from_okey(kp), c) >= vt;
+  const unsigned b = __ballot_sync(FULLMASK, ge);
+  if (inside && b != 0u && b != FULLMASK &&
+      (b >> (__ffs(b) - 1)) == (FULLMASK >> (__ffs(b) - 1)))
+    return from_okey(k0 - 16u + (uint32_t)(__ffs(b) - 1));  // the flip lies inside the window
+  // outside the window (extreme temperatures, subnormals): binary search over ordered keys
+  uint32_t lo = okey(-INFINITY), hi = okey(INFINITY);
+  if (vf(from_okey(lo), c) >= vt) return -INFINITY;
+  while (hi - lo > 1) {
+    const uint32_t mid = lo + (hi - lo) / 2;
+    if (vf(from_okey(mid), c) >= vt) hi = mid; else lo = mid;
+  }
+  return from_okey(hi);
+}
+
+// append a candidate to the run's buffer (overflow is flagged, never written past the end)
+__device__ __forceinline__ void add_cand(Smem& S, unsigned long long e) {
+  const int pos = atomicAdd(&S.sc[SC_NC], 1);
+  if (pos < RUN_CAP) S.cand[pos] = e;
+}
+
+// Sorts the run's candidates and keeps the K largest with every tie of the K-th: the kept
+// entries land sorted in out[0, n_ret). Returns n_ret; *tkey receives the K-th key (0 when all
+// n candidates are kept because n < K). The candidates stay untouched.
+__device__ int select_sorted(Smem& S, int n, int K, unsigned long long* out, uint32_t* tkey) {
+  const int tid = threadIdx.x;
+  if (n <= NT) {  // rank by counting: one candidate per thread
+    unsigned long long x = 0ull;
+    int rank = 0;
+    if (tid < n) {
+      x = S.cand[tid];
+      for (int j = 0; j < n; ++j) rank += S.cand[j] < x;
+      if (rank == K - 1) S.sc[SC_TKEY] = (int)comp_key(x);
+    }
+    cbar();
+    const uint32_t t = n >= K ? (uint32_t)S.sc[SC_TKEY] : 0u;
+    if (tid == 0) S.sc[SC_NRET] = 0;
+    cbar();
+    if (tid < n && comp_key(x) >= t) {
+      out[rank] = x;
+      atomicMax(&S.sc[SC_NRET], rank + 1);
+    }
+    cbar();
+    *tkey = t;
+    return S.sc[SC_NRET];
+  }
+  // larger sets (rare): bitonic sort of a padded copy, then cut at the K-th
+  int np = 1;
+  while (np < n) np <<= 1;
+  for (int j = tid; j < np; j += NT) out[j] = j < n ? S.cand[j] : ~0ull;
+  cbar();
+  for (int k = 2; k <= np; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < np; i += NT) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const unsigned long long a = out[i], b = out[ixj];
+          if ((a > b) == ((i & k) == 0)) {
+            out[i] = b;
+            out[ixj] = a;
+          }
+        }
+      }
+      cbar();
+    }
+  }
+  const uint32_t t = n >= K ? comp_key(out[K - 1]) : 0u;
+  *tkey = t;
+  return n >= K ? count_ge(out, n, t) : n;
+}
+
+// the elements of one staged vector at or above ylo become candidates
+template <typename TIn>
+__device__ __noinline__ void expand_vector(Smem& S, const RowCfg& c, const Geo& g, uint4 q, int j,
+                                           float ylo, bool checkbits) {
+  using E = Elem<TIn>;
+#pragma unroll 1
+  for (int e = 0; e < E::A; ++e) {
+    const int slot = j * E::A + e;
+    const int li = slot - g.off;
+    if (li < 0 || li >= g.n) continue;
+    if (checkbits && ((S.bitmap[slot >> 5] >> (slot & 31)) & 1u)) continue;
+    const float y = E::at(q, e);
+    if (y >= ylo) add_cand(S, comp(okey(vf(y, c)), (int)(g.gbase + li)));
+  }
+}
+
+struct RunState {        // per consumer thread, carried across the segments of a run
+  float m_t, s_t;        // online softmax max and sum (top-k off)
+  unsigned long long gbest;  // greedy: smallest composite key (max value, first index)
+};
+
+// One segment of the current run: penalties, then either the running greedy minimum, or the
+// candidates at or above the run's threshold (established on the run's first segment).
+template <typename TIn>
+__device__ void run_segment(const KParams& P, const RowCfg& c, const Geo& g, Stage& st, Smem& S,
+                            RunState& R) {
+  using E = Elem<TIn>;
+  constexpr int A = E::A;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  void* sv = st.data;
+  const int ns = st.ns;
+  if (ns < 0) {
+    if (tid == 0) S.sc[SC_RFL] |= RUN_OVER;
+    cbar();
+    return;
+  }
+  // ---- penalised tokens: exact float32 values on the side, -inf in the staged copy
+  if (ns > 0) {
+    const int nwords = (g.nvec * A + 31) / 32;
+    for (int wd = tid; wd < nwords; wd += NT) S.bitmap[wd] = 0u;
+    cbar();
+    for (int j = tid; j < ns; j += NT) {
+      const int cnt = st.side_cnt[j];
+      const int slot = g.off + (int)(st.side_id[j] - g.gbase);
+      if (cnt > 0) {
+        S.side_y[j] = penalize(E::sm(sv, slot), cnt, c);
+        atomicOr(&S.bitmap[slot >> 5], 1u << (slot & 31));
+        E::neg_inf(sv, slot);
+      } else {
+        S.side_y[j] = __int_as_float(0x7fc00000);  // NaN: not penalised, value stays in place
+      }
+    }
+    cbar();
+  }
+  const uint4* sv4 = (const uint4*)sv;
+  if (c.greedy) {  // running first argmax
+    float best = R.gbest == ~0ull ? -INFINITY : from_okey(comp_key(R.gbest));
+    for (int j = tid; j < g.nvec; j += NT) {
+      const uint4 q = sv4[j];
+      const float vm = E::vmax(q);
+      if (vm > best) {
+        int e = 0;
+        while (e < A - 1 && E::at(q, e) != vm) ++e;
+        const unsigned long long cc = comp(okey(vm), (int)(g.gbase + j * A + e - g.off));
+        R.gbest = cc < R.gbest ? cc : R.gbest;
+        best = vm;
+      }
+    }
+    for (int j = tid; j < ns; j += NT) {
+      const float y = S.side_y[j];
+      if (isnan(y)) continue;
+      const unsigned long long cc = comp(okey(y), st.side_id[j]);
+      R.gbest = cc < R.gbest ? cc : R.gbest;
+    }
+    cbar();
+    return;
+  }
+  const float ylo0 = S.sf[SF_YLO];
+  const bool known = !isnan(ylo0);  // the run's collection threshold exists
+  const bool checkbits = ns > 0;    // penalised slots hold -inf; only a -inf bound reaches them
+  float ylo = ylo0;
+  if (known) {
+    // ---- stream: each vector's maximum against the threshold; the rare vector that reaches
+    //      it is expanded in place by the thread that read it
+    for (int j = tid; j < g.nvec; j += NT) {
+      const uint4 q = sv4[j];
+      const float vm = E::vmax(q);
+      if (c.need_sum) {
+        if (vm > R.m_t) {
+          R.s_t *= ex2((R.m_t - vm) * c.c2);
+          R.m_t = vm;
+        }
+#pragma unroll
+        for (int e = 0; e < A; ++e) R.s_t += ex2((E::at(q, e) - R.m_t) * c.c2);
+      }
+      if (vm >= ylo) expand_vector<TIn>(S, c, g, q, j, ylo, checkbits && ylo == -INFINITY);
+    }
+    for (int j = tid; j < ns; j += NT) {
+      const float y = S.side_y[j];
+      if (isnan(y)) continue;
+      if (c.need_sum) {
+        if (y > R.m_t) {
+          R.s_t *= ex2((R.m_t - y) * c.c2);
+          R.m_t = y;
+        }
+        R.s_t += ex2((y - R.m_t) * c.c2);
+      }
+      if (y >= ylo) add_cand(S, comp(okey(vf(y, c)), st.side_id[j]));
+    }
+  } else {
+    // ---- first segment of the run: per-thread maxima, then a bound on the K-th largest
+    float tmax = -INFINITY;
+    for (int j = tid; j < g.nvec; j += NT) {
+      const uint4 q = sv4[j];
+      const float vm = E::vmax(q);
+      tmax = fmaxf(tmax, vm);
+      if (c.need_sum) {
+        if (vm > R.m_t) {
+          R.s_t *= ex2((R.m_t - vm) * c.c2);
+          R.m_t = vm;
+        }
+#pragma unroll
+        for (int e = 0; e < A; ++e) R.s_t += ex2((E::at(q, e) - R.m_t) * c.c2);
+      }
+    }
+    for (int j = tid; j < ns; j += NT) {
+      const float y = S.side_y[j];
+      if (isnan(y)) continue;
+      tmax = fmaxf(tmax, y);
+      if (c.need_sum) {
+        if (y > R.m_t) {
+          R.s_t *= ex2((R.m_t - y) * c.c2);
+          R.m_t = y;
+        }
+        R.s_t += ex2((y - R.m_t) * c.c2);
+      }
+    }
+    // each warp extracts its kw = ceil(K / 8) largest lane maxima (distinct elements); the
+    // K-th largest of those 8 * kw values bounds the segment's K-th largest value from below
+    const int kw = min((c.K + NCW - 1) / NCW, 32);
+    {
+      float mine = tmax;
+      for (int r = 0; r < kw; ++r) {
+        float m = mine;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(FULLMASK, m, o));
+        const unsigned b = __ballot_sync(FULLMASK, mine == m && m > -INFINITY);
+        if (lane == 0) S.ext[w * 32 + r] = b ? m : -INFINITY;
+        if (b && lane == __ffs(b) - 1) mine = -INFINITY;
+      }
+    }
+    if (tid == 0) S.sf[SF_TH] = -INFINITY;  // fewer than K finite values: no bound
+    cbar();
+    if (tid < NCW * kw) {
+      // rank of this value in the union of the eight descending lists (ties by list index)
+      const int wl = tid / kw, r = tid - wl * kw;
+      const float x = S.ext[wl * 32 + r];
+      int rank = r;
+      for (int o = 0; o < NCW; ++o) {
+        if (o == wl) continue;
+        const float* L = S.ext + o * 32;
+        int a = 0, b = kw;
+        while (a < b) {
+          const int mid = (a + b) >> 1;
+          if (o < wl ? (L[mid] >= x) : (L[mid] > x)) a = mid + 1; else b = mid;
+        }
+        rank += a;
+      }
+      if (rank == c.K - 1 && x > -INFINITY) S.sf[SF_TH] = x;
+    }
+    cbar();
+    if (w == 0) {
+      const float th = S.sf[SF_TH];
+      const float y = th == -INFINITY ? -INFINITY : ylo_for(vf(th, c), c);
+      if (lane == 0) S.sf[SF_YLO] = y;
+    }
+    cbar();
+    ylo = S.sf[SF_YLO];
+    for (int j = tid; j < g.nvec; j += NT) {
+      const uint4 q = sv4[j];
+      if (E::vmax(q) >= ylo) expand_vector<TIn>(S, c, g, q, j, ylo, checkbits && ylo == -INFINITY);
+    }
+    for (int j = tid; j < ns; j += NT) {
+      const float y = S.side_y[j];
+      if (y >= ylo) add_cand(S, comp(okey(vf(y, c)), st.side_id[j]));
+    }
+  }
+  cbar();
+  const int nc = S.sc[SC_NC];
+  if (nc > RUN_CAP) {
+    if (tid == 0) S.sc[SC_RFL] |= RUN_OVER;
+    cbar();
+    return;
+  }
+  // ---- tighten: whenever the buffer holds more than max(2K, 64) candidates (and after the
+  //      run's first segment), keep only the K largest (with ties) and raise the threshold to
+  //      the K-th value, so later segments contribute fewer candidates
+  if ((!known && nc > c.K) || nc > max(2 * c.K, 64)) {
+    unsigned long long* tmp = (unsigned long long*)st.data;  // the segment is done with
+    uint32_t t;
+    const int nr = select_sorted(S, nc, c.K, tmp, &t);
+    for (int j = tid; j < nr; j += NT) S.cand[j] = tmp[j];
+    if (tid == 0) S.sc[SC_NC] = nr;
+    if (w == 0) {
+      const float y = ylo_for(from_okey(t), c);
+      if (lane == 0) S.sf[SF_YLO] = y;
+    }
+    cbar();
+  }
+}
+
+// Completes the run: its sorted candidates become the row's answer (single-run rows), a shard
+// record (local mode), or a run record for the CTA that completes the row last to merge.
+template <typename TIn>
+__device__ void run_end(const KParams& P, const RowCfg& c, int row, int first_seg, int last_seg,
+                        Smem& S, RunState& R, unsigned char* scratch) {
+  const int tid = threadIdx.x;
+  const int nruns = seg_owner(P, row * P.nseg + P.nseg - 1) - seg_owner(P, row * P.nseg) + 1;
+  const int run_idx = blockIdx.x - seg_owner(P, row * P.nseg);
+  const int64_t lo = (int64_t)first_seg * P.seg_len;
+  const int64_t hi = min(P.V, (int64_t)(last_seg + 1) * P.seg_len);
+  const int n_run = (int)(hi - lo);
+  unsigned long long* sorted = (unsigned long long*)scratch;
+  // the run's own record, in shared memory first
+  uint32_t flags = 0, tkey = 0;
+  int nret = 0;
+  float m_y = -INFINITY, s_run = 0.f;
+  if (c.bad) {
+    flags = REC_BAD;
+  } else if (c.exact || (S.sc[SC_RFL] & RUN_OVER)) {
+    flags = c.exact ? REC_EXACT : REC_OVERFLOW;
+  } else if (c.greedy) {
+    const unsigned long long b = cta_min_u64(R.gbest, S);
+    if (b != ~0ull) {
+      sorted[0] = b;
+      nret = 1;
+      m_y = from_okey(comp_key(b));
+      tkey = comp_key(b);
+    }
+    if (n_run > 1) flags = REC_UNRETAINED;
+  } else {
+    const int nc = S.sc[SC_NC];
+    nret = select_sorted(S, nc, c.K, sorted, &tkey);
+    if (nret > CAND_CAP) flags = REC_OVERFLOW;
+    else if (nret < n_run) flags = REC_UNRETAINED;
+    else tkey = 0u;
+    if (c.need_sum) {  // rescale every partial sum to the run maximum, fixed order
+      const uint32_t mk = cta_max_u32(okey(R.m_t == -FLT_MAX ? -INFINITY : R.m_t), S);
+      m_y = from_okey(mk);
+      const float part = (R.m_t == -FLT_MAX) ? 0.f : R.s_t * ex2((R.m_t - m_y) * c.c2);
+      float tot;
+      cta_excl_scan_f(part, &tot, S);
+      s_run = tot;
+    }
+  }
+  cbar();
+  if (nruns == 1 && P.mode == 0) {  // the whole row is here: answer it directly
+    if (flags & REC_BAD) {
+      if (tid == 0) {
+        write_state(P, row, 3, -1, 0.f, 0.f, 0u, 0);
+        status_or(P, VINFER_ST_BAD_PARAM);
+      }
+      return;
+    }
+    bool done = false;
+    if (!(flags & (REC_OVERFLOW | REC_EXACT))) {
+      MergeIn m;
+      m.m_y = m_y;
+      m.s = s_run;
+      m.d_key = tkey;
+      m.flags = flags;
+      m.n = nret;
+      done = finalize_sorted(P, c, row, m, sorted, S);
+    }
+    cbar();
+    if (!done) exact_row<TIn>(P, c, row, S, scratch);
+    return;
+  }
+  // write the record: this run's slot of the row, or this rank's shard record (single run)
+  const bool shard = nruns == 1;  // local mode with the whole row here
+  unsigned char* rec = shard ? P.shard_out + (size_t)row * P.shard_stride
+                             : P.recs + ((size_t)row * P.nseg + run_idx) * REC_STRIDE;
+  const int cap = shard ? P.shard_cap : CAND_CAP;
+  if (nret > cap && !(flags & (REC_BAD | REC_EXACT))) flags = REC_OVERFLOW;
+  RecHdr* h = (RecHdr*)rec;
+  unsigned long long* ent = (unsigned long long*)(rec + sizeof(RecHdr));
+  const bool listed = !(flags & (REC_BAD | REC_EXACT | REC_OVERFLOW));
+  if (listed)
+    for (int j = tid; j < nret; j += NT) ent[j] = sorted[j];
+  if (tid == 0) {
+    h->m_y = m_y;
+    h->s = s_run;
+    h->n = listed ? nret : 0;
+    h->t_key = listed ? tkey : 0u;
+    h->flags = flags;
+  }
+  if (shard) return;
+  // the CTA that completes the row merges it
+  __threadfence();
+  cbar();
+  if (tid == 0) {
+    const int old = atom_add_acq_rel(&P.counters[row], 1);
+    const int last = old == nruns - 1;
+    if (last) P.counters[row] = 0;  // ready for the next call
+    S.sc[SC_LAST] = last;
+  }
+  cbar();
+  if (!S.sc[SC_LAST]) return;
+  finish_row<TIn>(P, S, scratch, row, P.recs + (size_t)row * P.nseg * REC_STRIDE, REC_STRIDE,
+                  nruns, P.mode == 1, nullptr);
+}
+
+template <typename TIn>
+__device__ void consumer(const KParams& P, Smem& S) {
+  const int tid = threadIdx.x;
+  const int s0 = seg_begin(P, blockIdx.x), s1 = seg_begin(P, blockIdx.x + 1);
+  RowCfg c{};
+  RunState R{};
+  int first_seg = 0;
+  for (int i = 0; s0 + i < s1; ++i) {
+    const int sg = s0 + i, row = sg / P.nseg, seg = sg - row * P.nseg;
+    const int s = i % NSTAGE, use = i / NSTAGE;
+    Stage& st = S.st[s];
+    const bool ok = mbar_wait_bounded(&S.full[s], use & 1);
+    if (cbar_or(!ok)) {
+      mbar_wait_bounded(&S.full[s], use & 1);  // a copy may still be in flight
+      if (tid == 0) status_or(P, VINFER_ST_TIMEOUT);
+      return;
+    }
+    if (i == 0 || seg == 0) {  // a new run
+      c = cfg_from(P, st.prm);
+      R.m_t = -FLT_MAX;
+      R.s_t = 0.f;
+      R.gbest = ~0ull;
+      first_seg = seg;
+      if (tid == 0) {
+        S.sc[SC_NC] = 0;
+        S.sc[SC_RFL] = 0;
+        S.sf[SF_YLO] = __int_as_float(0x7fc00000);  // NaN: no threshold yet
+      }
+      cbar();
+    }
+    if (!(c.bad || c.exact) && !(S.sc[SC_RFL] & RUN_OVER)) {
+      const Geo g = geometry<TIn>(P, row, seg);
+      run_segment<TIn>(P, c, g, st, S, R);  // ends with a consumer barrier
+    }
+    if (sg + 1 == s1 || seg == P.nseg - 1) {
+      run_end<TIn>(P, c, row, first_seg, seg, S, R, st.data);
+      cbar();
+    }
+    if (tid == 0) mbar_arrive(&S.empty[s]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// kernels
+// ---------------------------------------------------------------------------------------------
+template <typename TIn>
+__global__ void __launch_bounds__(NTHR, 2) k_sample(const KParams P) {
+  extern __shared__ __align__(128) unsigned char smraw[];
+  Smem& S = *reinterpret_cast<Smem*>(smraw);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x >= NT) {
+    producer<TIn>(P, S);
+    return;
+  }
+  consumer<TIn>(P, S);
+}
+
+// merge of gathered shard records: one CTA of consumer threads per row
+template <typename TIn>
+__global__ void __launch_bounds__(NT, 1) k_merge(const KParams P, const unsigned char* recs,
                                               int world, int* unresolved) {
   extern __shared__ __align__(128) unsigned char smraw[];
   Smem& S = *reinterpret_cast<Smem*>(smraw);
   const int row = blockIdx.x;
-  const RowCfg c = load_row(P, row);
-  const MergeIn m =
-      gather_records(recs + (size_t)row * P.shard_stride, (size_t)P.B * P.shard_stride, world,
-                     c, S);
-  bool done = false;
-  if (m.flags & REC_BAD) {
-    if (threadIdx.x == 0) {
-      P.out_ids[row] = -1;
-      status_or(P, VINFER_ST_BAD_PARAM);
-      RowState st = {};
-      st.kind = 3;
-      st.token = -1;
-      P.rows[row] = st;
-    }
-    done = true;
-  } else if (!(m.flags & (REC_OVERFLOW | REC_EXACT)) && m.n <= MERGE_CAP) {
-    done = finalize_sorted(P, c, row, m, S);
-  }
-  if (threadIdx.x == 0) {
-    if (unresolved) unresolved[row] = done ? 0 : 1;
-    if (!done) {
-      P.out_ids[row] = -1;
-      RowState st = {};
-      st.kind = 3;
-      st.token = -1;
-      P.rows[row] = st;
-    }
-  }
+  finish_row<TIn>(P, S, S.st[0].data, row, recs + (size_t)row * P.shard_stride,
+                  (size_t)P.B * P.shard_stride, world, false, unresolved);
 }
 
 // final probabilities [B, V] from the row states (parity checks only)
 template <typename TIn>
-__global__ void __launch_bounds__(NT) k_probs(const KParams P) {
+__global__ void __launch_bounds__(256) k_probs(const KParams P) {
   const int row = blockIdx.y;
   const RowCfg c = load_row(P, row);
   const RowState st = P.rows[row];
@@ -1436,7 +1736,8 @@ __global__ void __launch_bounds__(NT) k_probs(const KParams P) {
     hb = P.hrow[row + 1];
   }
   const float inv = st.s_kept > 0.f ? 1.0f / st.s_kept : 0.f;
-  for (int64_t i = (int64_t)blockIdx.x * NT + threadIdx.x; i < P.V; i += (int64_t)gridDim.x * NT) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < P.V;
+       i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t gid = P.voff + i;
     float q = 0.f;
     if (st.kind == 2) {
@@ -1450,7 +1751,8 @@ __global__ void __launch_bounds__(NT) k_probs(const KParams P) {
       }
       const float v = vf(y, c);
       const uint32_t key = okey(v);
-      bool keep = st.kind == 1 || key > st.cut_key || (key == st.cut_key && gid <= st.cut_id);
+      const bool keep =
+          st.kind == 1 || key > st.cut_key || (key == st.cut_key && gid <= st.cut_id);
       if (keep) q = ex2((v - st.m_v) * LOG2E) * inv;
     }
     out[i] = q;
@@ -1461,17 +1763,22 @@ __global__ void __launch_bounds__(NT) k_probs(const KParams P) {
 // host side
 // ---------------------------------------------------------------------------------------------
 struct Shape {
-  int nseg, seg_len;
+  int nseg, seg_len, grid;
 };
 
-Shape choose_shape(int64_t B, int64_t V, int dtype) {
+// Segments per row and CTAs for a batch. With fewer rows than CTAs, each row is split into
+// c = ctas / B runs of whole segments (nseg a multiple of c), so every CTA streams one run and
+// only split rows need a merge; with more rows than CTAs, the CTAs share the row-major list of
+// segments in equal contiguous ranges.
+Shape plan(int64_t B, int64_t V, int dtype, int ctas) {
   const int es = dtype == VINFER_DTYPE_BF16 ? 2 : 4;
   const int A = 16 / es;
   const int64_t min_seg = (V * es + SEG_BYTES - 1) / SEG_BYTES;
-  const int64_t target_ctas = 2048;
-  int64_t want = (target_ctas + B - 1) / B;
-  want = std::min<int64_t>(want, (V + 2047) / 2048);
-  int64_t nseg = std::max<int64_t>(min_seg, std::max<int64_t>(want, 1));
+  int64_t c = 1;
+  if (B < ctas) c = std::min<int64_t>(ctas / B, MAX_NSEG);
+  c = std::max<int64_t>(1, std::min<int64_t>(c, V / 2048));  // segments of >= 2048 tokens
+  int64_t nseg = std::max<int64_t>(min_seg, c);
+  nseg = (nseg + c - 1) / c * c;
   nseg = std::min<int64_t>(nseg, MAX_NSEG);
   int64_t len = (V + nseg - 1) / nseg;
   len = (len + A - 1) / A * A;
@@ -1479,6 +1786,8 @@ Shape choose_shape(int64_t B, int64_t V, int dtype) {
   Shape s;
   s.nseg = (int)nseg;
   s.seg_len = (int)len;
+  const int64_t total = B * nseg;
+  s.grid = (int)std::min<int64_t>(total, B < ctas ? B * c : ctas);
   return s;
 }
 
@@ -1488,13 +1797,16 @@ size_t align_up(size_t x) { return (x + ALIGN - 1) / ALIGN * ALIGN; }
 struct WsLayout {
   size_t counters, rows, recs, total;
 };
+// Records: one slot per (row, run). Rows are split into at most nseg runs; nseg is at most
+// MAX_NSEG when rows may be split for parallelism (B below the resident-CTA bound), otherwise
+// the count the segment size alone needs.
 WsLayout ws_layout(int64_t B, int64_t V, int dtype) {
-  const Shape s = choose_shape(B, V, dtype);
+  const int64_t nseg = B < CTA_CAP ? MAX_NSEG : plan(B, V, dtype, CTA_CAP).nseg;
   WsLayout L;
   L.counters = 0;
   L.rows = align_up((size_t)B * sizeof(int));
   L.recs = L.rows + align_up((size_t)B * sizeof(RowState));
-  L.total = L.recs + (size_t)B * s.nseg * REC_STRIDE;
+  L.total = L.recs + (size_t)B * nseg * REC_STRIDE;
   return L;
 }
 
@@ -1521,6 +1833,8 @@ KParams make_params(const VinferSampleArgs* a, const Shape& s, void* ws) {
   P.B = (int)a->batch;
   P.nseg = s.nseg;
   P.seg_len = s.seg_len;
+  P.total = (int)(a->batch * s.nseg);
+  P.grid = s.grid;
   P.flags = a->flags;
   P.temperature = a->temperature;
   P.top_k = a->top_k;
@@ -1544,37 +1858,57 @@ KParams make_params(const VinferSampleArgs* a, const Shape& s, void* ws) {
   return P;
 }
 
-// opt in to the dynamic shared memory of a kernel, once per device and kernel
-int set_smem(const void* kern, int slot) {
-  static bool done[64][4] = {};
+// per device and kernel: opt in to the dynamic shared memory once, and remember how many
+// CTAs of it fit on the device at once
+struct KernInfo {
+  bool ready;
+  int ctas;
+};
+int kernel_info(const void* kern, int slot, int threads, int* ctas) {
+  static KernInfo info[64][4] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VINFER_E_CUDA;
-  if (done[dev][slot]) return VINFER_OK;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)sizeof(Smem)) != cudaSuccess)
+  KernInfo& k = info[dev][slot];
+  if (!k.ready) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(Smem)) != cudaSuccess)
+      return VINFER_E_CUDA;
+    int sms = 0, per_sm = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return VINFER_E_CUDA;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, sizeof(Smem)) !=
+        cudaSuccess)
+      return VINFER_E_CUDA;
+    k.ctas = std::max(1, sms * per_sm);
+    k.ready = true;
+  }
+  *ctas = k.ctas;
+  return VINFER_OK;
+}
+
+// resident CTAs of k_sample on the current device (at most CTA_CAP)
+int sample_ctas(int dtype, int* ctas) {
+  const void* kern = dtype == VINFER_DTYPE_BF16 ? (const void*)k_sample<__nv_bfloat16>
+                                                : (const void*)k_sample<float>;
+  if (kernel_info(kern, dtype == VINFER_DTYPE_BF16 ? 0 : 1, NTHR, ctas) != VINFER_OK)
     return VINFER_E_CUDA;
-  done[dev][slot] = true;
+  *ctas = std::min(*ctas, CTA_CAP);
   return VINFER_OK;
 }
 
 int launch_sample(const KParams& P, int dtype, cudaStream_t st) {
-  const dim3 grid(P.nseg, P.B);
-  if (dtype == VINFER_DTYPE_BF16) {
-    if (set_smem((const void*)k_sample<__nv_bfloat16>, 0) != VINFER_OK) return VINFER_E_CUDA;
-    k_sample<__nv_bfloat16><<<grid, NT, sizeof(Smem), st>>>(P);
-  } else {
-    if (set_smem((const void*)k_sample<float>, 1) != VINFER_OK) return VINFER_E_CUDA;
-    k_sample<float><<<grid, NT, sizeof(Smem), st>>>(P);
-  }
+  const dim3 grid(P.grid);
+  if (dtype == VINFER_DTYPE_BF16) k_sample<__nv_bfloat16><<<grid, NTHR, sizeof(Smem), st>>>(P);
+  else k_sample<float><<<grid, NTHR, sizeof(Smem), st>>>(P);
   return cudaGetLastError() == cudaSuccess ? VINFER_OK : VINFER_E_CUDA;
 }
 
 int launch_probs(const KParams& P, int dtype, cudaStream_t st) {
   if (!P.out_probs) return VINFER_OK;
-  const int bx = (int)std::min<int64_t>(64, (P.V + NT * 8 - 1) / (NT * 8));
+  const int bx = (int)std::min<int64_t>(64, (P.V + 256 * 8 - 1) / (256 * 8));
   const dim3 grid(std::max(bx, 1), P.B);
-  if (dtype == VINFER_DTYPE_BF16) k_probs<__nv_bfloat16><<<grid, NT, 0, st>>>(P);
-  else k_probs<float><<<grid, NT, 0, st>>>(P);
+  if (dtype == VINFER_DTYPE_BF16) k_probs<__nv_bfloat16><<<grid, 256, 0, st>>>(P);
+  else k_probs<float><<<grid, 256, 0, st>>>(P);
   return cudaGetLastError() == cudaSuccess ? VINFER_OK : VINFER_E_CUDA;
 }
 
@@ -1607,7 +1941,9 @@ int vinfer_sample(const VinferSampleArgs* a, void* workspace, size_t workspace_b
   if (a->vocab_offset != 0 || a->vocab_total != a->vocab) return VINFER_E_ARG;
   if (!workspace) return VINFER_E_ARG;
   if (workspace_bytes < ws_layout(a->batch, a->vocab, a->dtype).total) return VINFER_E_LIMIT;
-  const Shape s = choose_shape(a->batch, a->vocab, a->dtype);
+  int ctas = 0;
+  if (sample_ctas(a->dtype, &ctas) != VINFER_OK) return VINFER_E_CUDA;
+  const Shape s = plan(a->batch, a->vocab, a->dtype, ctas);
   KParams P = make_params(a, s, workspace);
   P.mode = 0;
   cudaStream_t st = (cudaStream_t)stream;
@@ -1627,7 +1963,9 @@ int vinfer_sample_local(const VinferSampleArgs* a, int32_t record_cap, void* rec
   if (rc != VINFER_OK) return rc;
   if (!records || !workspace || record_cap < 1 || record_cap > CAND_CAP) return VINFER_E_ARG;
   if (workspace_bytes < ws_layout(a->batch, a->vocab, a->dtype).total) return VINFER_E_LIMIT;
-  const Shape s = choose_shape(a->batch, a->vocab, a->dtype);
+  int ctas = 0;
+  if (sample_ctas(a->dtype, &ctas) != VINFER_OK) return VINFER_E_CUDA;
+  const Shape s = plan(a->batch, a->vocab, a->dtype, ctas);
   KParams P = make_params(a, s, workspace);
   P.mode = 1;
   P.shard_out = (unsigned char*)records;
@@ -1646,15 +1984,23 @@ int vinfer_sample_merge(const VinferSampleArgs* a, int32_t record_cap, const voi
     return VINFER_E_ARG;
   if (world_size * record_cap > MERGE_CAP) return VINFER_E_LIMIT;
   if (workspace_bytes < ws_layout(a->batch, a->vocab, a->dtype).total) return VINFER_E_LIMIT;
-  const Shape s = choose_shape(a->batch, a->vocab, a->dtype);
+  const Shape s = plan(a->batch, a->vocab, a->dtype, 1);
   KParams P = make_params(a, s, workspace);
   P.mode = 2;
   P.shard_cap = record_cap;
   P.shard_stride = vinfer_sample_record_bytes(record_cap);
   cudaStream_t st = (cudaStream_t)stream;
-  if (set_smem((const void*)k_merge, 2) != VINFER_OK) return VINFER_E_CUDA;
-  k_merge<<<(unsigned)a->batch, NT, sizeof(Smem), st>>>(P, (const unsigned char*)records,
-                                                        world_size, unresolved);
+  const void* kern = a->dtype == VINFER_DTYPE_BF16 ? (const void*)k_merge<__nv_bfloat16>
+                                                   : (const void*)k_merge<float>;
+  int ctas = 0;
+  if (kernel_info(kern, a->dtype == VINFER_DTYPE_BF16 ? 2 : 3, NT, &ctas) != VINFER_OK)
+    return VINFER_E_CUDA;
+  if (a->dtype == VINFER_DTYPE_BF16)
+    k_merge<__nv_bfloat16><<<(unsigned)a->batch, NT, sizeof(Smem), st>>>(
+        P, (const unsigned char*)records, world_size, unresolved);
+  else
+    k_merge<float><<<(unsigned)a->batch, NT, sizeof(Smem), st>>>(
+        P, (const unsigned char*)records, world_size, unresolved);
   if (cudaGetLastError() != cudaSuccess) return VINFER_E_CUDA;
   return launch_probs(P, a->dtype, st);
 }
