@@ -118,6 +118,24 @@ int vinfer_sample_merge(const VinferSampleArgs* args, int32_t record_cap, const 
                         int32_t world_size, int32_t* unresolved, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* ---- allocation-free variant ---------------------------------------------------------------
+ * No counterpart in the reference: an addition of this library. Some callers cannot allocate
+ * device memory when they sample: a serving engine that has handed nearly all of HBM to its
+ * KV-cache pool at start-up (a cudaMalloc then fails, or waits for the device), or a host
+ * that links only this C library and owns no device allocator (a Go, Java or C runtime).
+ * vinfer_sample_static is vinfer_sample without the workspace argument: its scratch is a
+ * fixed array of VINFER_STATIC_SCRATCH_BYTES compiled into the library, which every device
+ * that loads the library holds until the process exits. It allocates nothing.
+ *  - Limit: the call returns VINFER_E_LIMIT when vinfer_sampler_workspace_bytes(batch, vocab,
+ *    dtype) exceeds VINFER_STATIC_SCRATCH_BYTES (up to 63 rows fit at any vocabulary).
+ *  - The first call on a device looks up the array's device address on that device (which
+ *    may load the library's device code); make it before any stream capture.
+ *  - All calls on one device share the array: calls that can overlap on the GPU (different
+ *    streams or host threads without ordering) race and corrupt each other's results.
+ */
+#define VINFER_STATIC_SCRATCH_BYTES (32u << 20)
+int vinfer_sample_static(const VinferSampleArgs* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,6 +21,7 @@ ST_BAD_PARAM, ST_NONFINITE, ST_TIMEOUT, ST_INTERNAL = 1, 2, 4, 8
 FLAG_EXACT_ALL = 1
 MAX_VOCAB = 262144
 MAX_BATCH = 65535
+STATIC_SCRATCH_BYTES = 32 << 20
 
 EXPORTS = (
     "vinfer_sampler_abi_version",
@@ -30,6 +31,7 @@ EXPORTS = (
     "vinfer_sample_record_bytes",
     "vinfer_sample_local",
     "vinfer_sample_merge",
+    "vinfer_sample_static",
 )
 
 _ERRORS = {E_ARG: "invalid argument", E_LIMIT: "limit exceeded", E_CUDA: "CUDA error"}
@@ -94,6 +96,8 @@ def load() -> C.CDLL:
     lib.vinfer_sample_merge.restype = C.c_int
     lib.vinfer_sample_merge.argtypes = [C.POINTER(SampleArgs), C.c_int32, C.c_void_p, C.c_int32,
                                         C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
+    lib.vinfer_sample_static.restype = C.c_int
+    lib.vinfer_sample_static.argtypes = [C.POINTER(SampleArgs), C.c_void_p]
     version = lib.vinfer_sampler_abi_version()
     if version != ABI_VERSION:
         raise RuntimeError(f"sampler library ABI {version}, expected {ABI_VERSION}")

@@ -37,6 +37,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "vinfer_sampler.h"
 
@@ -2002,6 +2003,64 @@ int vinfer_sample_merge(const VinferSampleArgs* a, int32_t record_cap, const voi
     k_merge<float><<<(unsigned)a->batch, NT, sizeof(Smem), st>>>(
         P, (const unsigned char*)records, world_size, unresolved);
   if (cudaGetLastError() != cudaSuccess) return VINFER_E_CUDA;
+  return launch_probs(P, a->dtype, st);
+}
+
+}  // extern "C"
+
+// The allocation-free entry point, vinfer_sample_static, runs on this fixed scratch array
+// instead of a caller-allocated workspace. Every device that loads the library holds it until
+// the process exits. Host code must not hand the symbol itself to a kernel: on the host it
+// names a stand-in, not device memory. The device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_sample_scratch[VINFER_STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_scratch_mu;
+void* g_scratch_addr[64] = {};
+
+// Device address of g_sample_scratch on the current device, looked up on the first call there
+// (with that device current, as cudaGetSymbolAddress requires).
+int static_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VINFER_E_CUDA;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_sample_scratch) != cudaSuccess || !p) return VINFER_E_CUDA;
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return VINFER_OK;
+}
+}  // namespace
+
+extern "C" {
+
+// vinfer_sample without a caller workspace, for callers that cannot allocate device memory.
+// Allocates nothing: the scratch is the static array above; only kernels and one
+// cudaMemsetAsync are issued. Shapes whose workspace exceeds the array are refused with
+// VINFER_E_LIMIT. All calls on a device share the array, so calls that overlap on the GPU race.
+int vinfer_sample_static(const VinferSampleArgs* a, void* stream) {
+  int rc = check_args(a);
+  if (rc != VINFER_OK) return rc;
+  if (a->vocab_offset != 0 || a->vocab_total != a->vocab) return VINFER_E_ARG;
+  const WsLayout L = ws_layout(a->batch, a->vocab, a->dtype);
+  if (L.total > sizeof(g_sample_scratch)) return VINFER_E_LIMIT;
+  void* ws = nullptr;
+  if (static_scratch(&ws) != VINFER_OK) return VINFER_E_CUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  // The per-row arrival counters must start at zero. The array keeps whatever the previous
+  // call left, possibly for another shape whose records overlap these counters: clear them.
+  if (cudaMemsetAsync((unsigned char*)ws + L.counters, 0, (size_t)a->batch * sizeof(int), st) !=
+      cudaSuccess)
+    return VINFER_E_CUDA;
+  int ctas = 0;
+  if (sample_ctas(a->dtype, &ctas) != VINFER_OK) return VINFER_E_CUDA;
+  const Shape s = plan(a->batch, a->vocab, a->dtype, ctas);
+  KParams P = make_params(a, s, ws);
+  P.mode = 0;
+  rc = launch_sample(P, a->dtype, st);
+  if (rc != VINFER_OK) return rc;
   return launch_probs(P, a->dtype, st);
 }
 
