@@ -307,6 +307,154 @@ def bench_single(args) -> dict:
 
 
 # ----------------------------------------------------------------------------------------------
+# N > 1: configuration 4, vocab-sharded (one process per GPU, NCCL)
+# ----------------------------------------------------------------------------------------------
+def bench_sharded(args) -> dict | None:
+    from datetime import timedelta  # noqa: PLC0415
+
+    import torch.distributed as dist  # noqa: PLC0415
+
+    from vinfer_b200 import SAMPLER, BackendContext  # noqa: PLC0415
+    from vinfer_b200.sharded import B200ShardKernels, ShardedSampler, shard_range  # noqa: PLC0415
+    from vinfer_b200.workloads import config4_shard  # noqa: PLC0415
+
+    rank, world, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    try:
+        backend = SAMPLER.resolve("b200", BackendContext(dev, torch.bfloat16))
+        sampler = ShardedSampler(B200ShardKernels(backend))
+        B, V = 1024, 248_320
+        lo, hi = shard_range(V, world, rank)
+        x, params, u = config4_shard(rank, world, dev, B, V)
+        shard_bytes = x.numel() * x.element_size()
+        nbuf = max(2, int(np.ceil(2 * L2_BYTES / shard_bytes)) + 1)
+        bufs = [x] + [x.clone() for _ in range(nbuf - 1)]
+        out = torch.empty(B, dtype=torch.int32, device=dev)
+        stream = torch.cuda.current_stream(dev)
+
+        def step(i: int) -> None:
+            sampler.sample_batch(bufs[i % nbuf], params, u, None, V, out=out)
+
+        for i in range(max(args.warmup, 3)):
+            step(i)
+        torch.cuda.synchronize()
+        sampler.kernels.check()
+
+        clocks = Clocks(local) if rank == 0 else None
+        if clocks:
+            clocks.start()
+        unresolved = 0
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            step(i)
+            unresolved += sampler.last_unresolved
+        t1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ms = t0.elapsed_time(t1)
+        clk = clocks.stop() if clocks else None
+
+        # the local-record kernel alone: events around single launches on its stream
+        bufd = sampler._buffers(B, dev)
+        torch.cuda._sleep(20_000_000)
+        pairs = []
+        for i in range(16):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            sampler.kernels.local(bufs[i % nbuf], params, u, None, lo, V, sampler.record_cap,
+                                  bufd["local"], bufd["scratch_ids"])
+            e.record(stream)
+            pairs.append((s, e))
+        torch.cuda.synchronize()
+        local_ms = statistics.mean(s.elapsed_time(e) for s, e in pairs)
+
+        # end to end through the public API: this rank's shard and the row parameters copied
+        # from pinned host memory, the ids copied back, every step
+        host_x = x.cpu().pin_memory()
+        host_p = {k: getattr(params, k).cpu().pin_memory() for k in
+                  ("temperature", "top_k", "top_p", "min_p", "repetition_penalty",
+                   "presence_penalty", "frequency_penalty")}
+        host_u = u.cpu().pin_memory()
+        host_ids = torch.empty(B, dtype=torch.int32).pin_memory()
+        d_x = torch.empty_like(x)
+        d_u = torch.empty_like(u)
+        h2d = (host_x.numel() * host_x.element_size() + host_u.numel() * 4
+               + sum(t.numel() * t.element_size() for t in host_p.values()))
+
+        def e2e_step() -> None:
+            d_x.copy_(host_x, non_blocking=True)
+            for k, t in host_p.items():
+                getattr(params, k).copy_(t, non_blocking=True)
+            d_u.copy_(host_u, non_blocking=True)
+            ids = sampler.sample_batch(d_x, params, d_u, None, V, out=out)
+            host_ids.copy_(ids, non_blocking=True)
+
+        e2e_steps = max(3, min(args.steps, 20))
+        e2e_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
+        sampler.kernels.check()
+
+        t = torch.tensor([ms, local_ms, e2e_ms, float(unresolved)], dtype=torch.float64,
+                         device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, local_ms, e2e_ms, unresolved = float(t[0]), float(t[1]), float(t[2]), int(t[3])
+    finally:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    peak, kind = measured_peak()
+    shard_algo = B * (hi - lo) * 2 + 36 * B
+    achieved = shard_algo / (local_ms * 1e-3) / 1e9
+    return {
+        "metric": "sampled rows/sec (logits HBM GB/s as % of B200 peak in roofline)",
+        "value": B * args.steps / (ms * 1e-3),
+        "unit": "rows/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded on the device, configuration 4 distribution)",
+        "config": {"workload": "config4: batch 1024 x vocab 248320 bf16 N(0,3) + 4 spikes, "
+                               f"vocab-sharded over {world} GPUs, local top-k 50 records, NCCL "
+                               "all-gather, merge on every rank, temp 1, top-k 50, top-p 0.9",
+                   "batch": B, "vocab": V, "shard_vocab": hi - lo,
+                   "record_bytes_per_row": sampler.rec_bytes,
+                   "allgather_bytes_per_rank": B * sampler.rec_bytes,
+                   "l2": f"{nbuf} rotating shard buffers per rank "
+                         f"({nbuf * shard_bytes / 2**20:.0f} MiB > 2x L2)",
+                   "parallelism": f"vocab-sharded over {world} ranks",
+                   "unresolved_rows_in_timed_steps": unresolved},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": f"{kind} (copy bandwidth)",
+                     "traffic": None, "algorithmic_bytes": shard_algo,
+                     "kernel": "k_sample<bf16> (local records, rank 0 shard)",
+                     "kernel_ms": local_ms},
+        "clocks": clk,
+        "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "rows/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": B * 4, "steps": e2e_steps},
+        "gpu_launches": 2 * args.steps,
+        "cpu_baseline": None,
+    }
+
+
+# ----------------------------------------------------------------------------------------------
 # reference arm: vinfer's CPU sampler on this host
 # ----------------------------------------------------------------------------------------------
 def bench_reference(args, world: int) -> dict:
@@ -365,10 +513,11 @@ def main() -> None:
         if rank == 0:
             print(json.dumps(bench_reference(args, world)), flush=True)
         return
-    if world > 1 or args.gpus > 1:
-        from vinfer_b200.sharded import bench_sharded  # noqa: PLC0415
-
+    if world > 1:
         line = bench_sharded(args)
+    elif args.gpus > 1:
+        raise SystemExit("--gpus N > 1 runs one process per GPU: launch bench.py under "
+                         "torch.distributed.run with --nproc-per-node N")
     else:
         line = bench_single(args)
     if line is not None and rank == 0:

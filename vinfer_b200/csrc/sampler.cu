@@ -1188,7 +1188,9 @@ __device__ void producer(const KParams& P, Smem& S) {
       if (pen) {
         const int64_t a = __ldg(P.hrow + row);
         hend = __ldg(P.hrow + row + 1);
-        hp = seg == 0 ? a : warp_lower_bound(P.hids, a, hend, g.gbase, lane);
+        // the first entry at or after this segment's first global id (entries of lower
+        // vocabulary shards precede it when the row is sharded)
+        hp = (seg == 0 && P.voff == 0) ? a : warp_lower_bound(P.hids, a, hend, g.gbase, lane);
       }
     }
     // penalised tokens of this segment: the next entries of the row's ascending history
@@ -1379,8 +1381,11 @@ __device__ void run_segment(const KParams& P, const RowCfg& c, const Geo& g, Sta
     cbar();
     for (int j = tid; j < ns; j += NT) {
       const int cnt = st.side_cnt[j];
-      const int slot = g.off + (int)(st.side_id[j] - g.gbase);
-      if (cnt > 0) {
+      const int64_t li = (int64_t)st.side_id[j] - g.gbase;
+      const int slot = g.off + (int)li;
+      const bool inside = li >= 0 && li < g.n;  // false only for a history out of order
+      if (!inside) status_or(P, VINFER_ST_INTERNAL);
+      if (cnt > 0 && inside) {
         S.side_y[j] = penalize(E::sm(sv, slot), cnt, c);
         atomicOr(&S.bitmap[slot >> 5], 1u << (slot & 31));
         E::neg_inf(sv, slot);

@@ -177,3 +177,30 @@ def make(config: int, batch: int | None = None, vocab: int | None = None,
         raise ValueError(f"unknown configuration {config} (1..5)")
     w.meta["config"] = config
     return w
+
+
+def config4_shard(rank: int, world: int, device: torch.device, batch: int = 1024,
+                  vocab: int = 248_320, seed: int = 4):
+    """This rank's shard of configuration 4, generated on the device: N(0, 3) logits with 4
+    spikes of +10 per row at seeded global ids (the same ids on every rank), temperature 1,
+    top-k 50, top-p 0.9, one seeded uniform per row shared by all ranks. The values follow the
+    configuration's distribution; they are not the CPU generator's values."""
+    from vinfer_b200.sampling import RowParams  # noqa: PLC0415
+
+    lo, hi = vocab * rank // world, vocab * (rank + 1) // world
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1000 + rank)
+    x = torch.randn(batch, hi - lo, generator=g, device=device, dtype=torch.float32) * 3.0
+    gc = torch.Generator().manual_seed(seed)
+    spikes = torch.randint(vocab, (batch, 4), generator=gc)
+    uniforms = torch.rand(batch, generator=gc)
+    r, c = torch.nonzero((spikes >= lo) & (spikes < hi), as_tuple=True)
+    x[r.to(device), (spikes[r, c] - lo).to(device)] += 10.0
+    x = x.to(torch.bfloat16)
+    f = np.float32
+    params = RowParams.from_arrays(
+        device, temperature=np.full(batch, 1.0, f), top_k=np.full(batch, 50, np.int32),
+        top_p=np.full(batch, 0.9, f), min_p=np.zeros(batch, f),
+        repetition_penalty=np.ones(batch, f), presence_penalty=np.zeros(batch, f),
+        frequency_penalty=np.zeros(batch, f))
+    return x, params, uniforms.to(device)
