@@ -297,11 +297,12 @@ def bench_single(args) -> dict:
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": f"{peak_kind} (copy bandwidth)",
                      "traffic": traffic, "algorithmic_bytes": algo,
-                     "kernel": "k_sample<bf16>", "kernel_ms": kernel_ms},
+                     "kernel": "k_stream<bf16> + k_finish<bf16> (one sample_batch)",
+                     "kernel_ms": kernel_ms},
         "clocks": clk,
         "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "rows/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": B * 4, "steps": e2e_steps},
-        "gpu_launches": K,
+        "gpu_launches": 2 * K,  # k_stream and k_finish per step
         "cpu_baseline": cpu,
     }
 
@@ -416,7 +417,7 @@ def bench_sharded(args) -> dict | None:
     if rank != 0:
         return None
     peak, kind = measured_peak()
-    shard_algo = B * (hi - lo) * 2 + 36 * B
+    shard_algo = B * (hi - lo) * 2 + 36 * B  # local-record pass: this rank's logits and params
     achieved = shard_algo / (local_ms * 1e-3) / 1e9
     return {
         "metric": "sampled rows/sec (logits HBM GB/s as % of B200 peak in roofline)",
@@ -444,12 +445,12 @@ def bench_sharded(args) -> dict | None:
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": f"{kind} (copy bandwidth)",
                      "traffic": None, "algorithmic_bytes": shard_algo,
-                     "kernel": "k_sample<bf16> (local records, rank 0 shard)",
+                     "kernel": "k_stream<bf16> + k_finish<bf16> (local records, one rank)",
                      "kernel_ms": local_ms},
         "clocks": clk,
         "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "rows/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": B * 4, "steps": e2e_steps},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": 3 * args.steps,  # k_stream, k_finish (records), k_merge per step
         "cpu_baseline": None,
     }
 

@@ -73,16 +73,18 @@ def test_static_scratch_matches_the_workspace_entry_point():
 def test_shapes_beyond_the_static_scratch_are_refused():
     build()
     lib = _lib.load()
-    too_big = 64  # rows: 64 x 64 run records of 8 KiB exceed the 32 MiB array
-    assert (lib.vinfer_sampler_workspace_bytes(too_big, 151936, _lib.DTYPE_BF16)
-            > _lib.STATIC_SCRATCH_BYTES)
-    assert (lib.vinfer_sampler_workspace_bytes(too_big - 1, 262144, _lib.DTYPE_F32)
-            <= _lib.STATIC_SCRATCH_BYTES)
+    # the largest float32 vocabulary needs the most scratch per row; at least 63 rows fit
+    def ws(rows):
+        return lib.vinfer_sampler_workspace_bytes(rows, _lib.MAX_VOCAB, _lib.DTYPE_F32)
+    too_big = 63
+    while ws(too_big) <= _lib.STATIC_SCRATCH_BYTES:
+        too_big += 1
+    assert ws(too_big - 1) <= _lib.STATIC_SCRATCH_BYTES < ws(too_big)
     a = _lib.SampleArgs()
     a.logits = 256
     a.out_ids = 256
-    a.dtype = _lib.DTYPE_BF16
-    a.batch, a.vocab, a.ld, a.vocab_total = too_big, 151936, 151936, 151936
+    a.dtype = _lib.DTYPE_F32
+    a.batch, a.vocab, a.ld, a.vocab_total = too_big, _lib.MAX_VOCAB, _lib.MAX_VOCAB, _lib.MAX_VOCAB
     # refused before any CUDA call: this runs without a GPU
     assert lib.vinfer_sample_static(C.byref(a), None) == _lib.E_LIMIT
     with pytest.raises(RuntimeError, match="limit exceeded"):

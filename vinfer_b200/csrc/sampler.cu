@@ -46,35 +46,31 @@ namespace {
 // ---------------------------------------------------------------------------------------------
 // configuration
 // ---------------------------------------------------------------------------------------------
-constexpr int NCW = 8;                  // consumer warps
-constexpr int NT = NCW * 32;            // consumer threads
-constexpr int NSTAGE = 2;               // shared-memory stages
-constexpr int NTHR = NT + 32;           // threads per CTA: consumers + one producer warp
-constexpr int SEG_BYTES = 32768;        // largest segment held in a stage
-constexpr int SBUF_BYTES = SEG_BYTES + 64;
-constexpr int SIDE_CAP = 512;           // penalised tokens per segment
-constexpr int SIDE_PER_LANE = SIDE_CAP / 32;
+constexpr int NCW = 8;                  // warps per CTA
+constexpr int NT = NCW * 32;            // threads per CTA
+constexpr int U = 8;                    // 16-byte vectors a thread loads per segment
+constexpr int SEG_BYTES = NT * U * 16;  // 32 KiB: one round of loads of the CTA
+constexpr int CAND_BUF = 2048;          // candidates held for the run being processed
+constexpr int SCRATCH = 4096;           // 8-byte words of the scratch region (32 KiB)
+constexpr int HIST_CAP = SCRATCH;       // history entries of a run staged in scratch
 constexpr int CAND_CAP = 1024;          // entries of one record
-constexpr int RUN_CAP = 2048;           // candidates held for the run being processed
-constexpr int CTA_CAP = 320;            // resident CTAs assumed when sizing workspaces
-constexpr int KMAX = 256;               // largest top-k served by the candidate path
-constexpr int KC = 64;                  // candidates kept per segment when top-k is off
+constexpr int KMAX = 192;               // largest top-k served by the candidate path
+constexpr int KC = 64;                  // candidates kept per run when top-k is off
 constexpr int MAX_NSEG = 64;
-constexpr int MERGE_CAP = 2048;         // merged entries (input in cand, sorted copy in a stage)
-constexpr int BM_WORDS = (SBUF_BYTES / 2 + 31) / 32 + 2;
+constexpr int CTA_CAP = 1024;          // resident CTAs assumed when sizing workspaces
+constexpr int MERGE_CAP = 2048;         // merged entries (input in cand, sorted in scratch)
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr double FX_ONE = 17592186044416.0;      // 2^44: fixed-point unit of probability mass
-constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz: bound on any wait
 constexpr unsigned FULLMASK = 0xffffffffu;
 
-static_assert(NT == 256, "block helpers assume 256 consumer threads");
-static_assert(KMAX <= 8 * 32, "warp extraction covers at most 8 x 32 values");
-static_assert(MERGE_CAP * 8 <= SEG_BYTES, "a stage holds the sorted merge");
+static_assert(NT == 256, "block helpers assume 256 threads");
+static_assert(KMAX <= NCW * 32, "warp extraction covers at most 8 x 32 values");
+static_assert(KC <= 64, "block tightening ranks 64 delegates");
+static_assert(MERGE_CAP <= CAND_BUF && MERGE_CAP <= SCRATCH, "merge input and output fit");
 static_assert((int64_t)VINFER_MAX_VOCAB * 4 <= (int64_t)MAX_NSEG * SEG_BYTES,
               "the largest float32 row fits MAX_NSEG segments");
-static_assert(MERGE_CAP <= RUN_CAP, "the candidate buffer holds the merge input");
-static_assert((size_t)VINFER_MAX_VOCAB / 8 <= (size_t)RUN_CAP * 8 + SEG_BYTES,
-              "the exact search's row bitmap spans the candidate buffer and a stage");
+static_assert((CAND_BUF * 2 + SCRATCH * 2) * 32 >= VINFER_MAX_VOCAB,
+              "the exact search's row bitmap fits the candidate and scratch regions");
 
 // record flags
 constexpr uint32_t REC_UNRETAINED = 1u;  // elements below t_key exist that are not listed
@@ -133,22 +129,13 @@ struct KParams {
   size_t shard_stride;
 };
 
-struct __align__(16) Stage {
-  unsigned char data[SBUF_BYTES];  // the segment; merge / exact search scratch afterwards
-  int32_t side_id[SIDE_CAP];       // penalised tokens of the segment (global ids) ...
-  int32_t side_cnt[SIDE_CAP];      // ... and their counts
-  float prm[8];                    // T, top_p, min_p, rep, pres, freq, uniform, top_k (bits)
-  int32_t ns;                      // side entries, -1 when more than SIDE_CAP
-  int32_t pad[3];
-};
-
 struct __align__(16) Smem {
-  Stage st[NSTAGE];
-  unsigned long long cand[RUN_CAP];   // candidates of the run (composite keys); exact: bins
-  float side_y[SIDE_CAP];             // penalised values of the current item
-  uint32_t bitmap[BM_WORDS];          // penalised slots of the current item
-  float ext[NT];                      // lane maxima extracted per warp
-  unsigned long long bin_mass[256];   // exact search: radix bins
+  unsigned long long cand[CAND_BUF];   // run candidates (composite keys), sorted in place;
+                                       // merge input; exact search: row bitmap words
+  unsigned long long scratch[SCRATCH]; // the run's history entries while streaming; merge
+                                       // output; exact search: more row bitmap words
+  float ext[NT];                       // lane maxima extracted per warp
+  unsigned long long bin_mass[256];    // exact search: radix bins
   uint32_t bin_cnt[256];
   RecHdr mh[MAX_NSEG];
   int moff[MAX_NSEG + 1];
@@ -157,15 +144,18 @@ struct __align__(16) Smem {
   int redi[NCW + 1];
   int sc[16];
   float sf[8];
-  unsigned long long full[NSTAGE];
-  unsigned long long empty[NSTAGE];
+  int64_t hpos;                        // first history entry of the run
+  int wcnt[NCW];                       // candidates per warp slice at the end of a run
+  uint32_t ylo_key;                    // the run's threshold: ordered key of a raw logit
+  unsigned long long dkth;             // the run's K-th largest unflagged delegate
+  int rhi[MAX_NSEG];                   // k_finish: end (global id) of each run of the row
 };
 
 // scalar slots in Smem::sc / Smem::sf
-enum { SC_NC = 0, SC_NRET, SC_TKEY, SC_LAST, SC_B, SC_J, SC_X0, SC_X1, SC_NQ, SC_RFL };
+enum { SC_NC = 0, SC_NRET, SC_TKEY, SC_LAST, SC_B, SC_J, SC_X0, SC_X1, SC_NQ, SC_RFL, SC_NH };
 // run flags in Smem::sc[SC_RFL]
-constexpr int RUN_OVER = 1;  // a side list or the candidate buffer overflowed
-enum { SF_TH = 0, SF_YLO, SF_SK, SF_M };
+constexpr int RUN_OVER = 1;  // the candidate buffer overflowed
+enum { SF_TH = 0, SF_SK = 2, SF_M };
 
 // ---------------------------------------------------------------------------------------------
 // small device helpers
@@ -190,13 +180,10 @@ __device__ __forceinline__ unsigned long long comp(uint32_t key, int id) {
 __device__ __forceinline__ uint32_t comp_key(unsigned long long c) { return ~(uint32_t)(c >> 32); }
 __device__ __forceinline__ int comp_id(unsigned long long c) { return (int)(uint32_t)c; }
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
 __device__ __forceinline__ void status_or(const KParams& P, uint32_t bits) {
   if (P.status) atomicOr(reinterpret_cast<unsigned int*>(P.status), bits);
 }
-// barrier of the consumer warps only (the producer warps run their own loop)
+// CTA barrier (named barrier 1 over all threads)
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
 __device__ __forceinline__ bool cbar_or(bool p) {
   uint32_t r;
@@ -213,51 +200,6 @@ __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
   asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
                : "memory");
   return old;
-}
-
-// ---- TMA bulk copy (global -> shared) with an mbarrier, waits bounded -----------------------
-__device__ __forceinline__ void mbar_init(unsigned long long* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_fence_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes,
-                                            unsigned long long* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Wait for phase `parity` of `bar`, giving up after WAIT_CYCLES. Returns false on timeout.
-// try_wait suspends the warp in hardware until the phase completes or a short time limit.
-__device__ bool mbar_wait_bounded(unsigned long long* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > WAIT_CYCLES) return false;
-  }
-  return true;
 }
 
 // ---- element access ---------------------------------------------------------------------------
@@ -312,33 +254,6 @@ struct Elem<__nv_bfloat16> {
     return __uint_as_float((e & 1) ? (w & 0xFFFF0000u) : (w << 16));
   }
 };
-
-// segment geometry: local index i lives at slot off + i of the stage buffer
-struct Geo {
-  int64_t lo, gbase;
-  int n, head, inter, tail0, off, nvec, pad_end;
-  const void* rowp;
-};
-template <typename TIn>
-__device__ Geo geometry(const KParams& P, int row, int seg) {
-  constexpr int A = Elem<TIn>::A;
-  constexpr int ES = 16 / A;
-  Geo g;
-  g.lo = (int64_t)seg * P.seg_len;
-  const int64_t hi = min(P.V, g.lo + (int64_t)P.seg_len);
-  g.n = (int)(hi - g.lo);
-  g.rowp = (const TIn*)P.logits + (int64_t)row * P.ld;
-  const uintptr_t gaddr = (uintptr_t)((const TIn*)g.rowp + g.lo);
-  g.head = (int)(((16u - (uint32_t)(gaddr & 15u)) & 15u) / ES);
-  if (g.head > g.n) g.head = g.n;
-  g.inter = (int)((((int64_t)(g.n - g.head) * ES) / 16) * 16 / ES);
-  g.tail0 = g.head + g.inter;
-  g.off = (A - g.head % A) % A;
-  g.nvec = (g.off + g.n + A - 1) / A;
-  g.pad_end = g.nvec * A - (g.off + g.n);
-  g.gbase = P.voff + g.lo;
-  return g;
-}
 
 // ---------------------------------------------------------------------------------------------
 // per-row configuration
@@ -655,7 +570,7 @@ __device__ void write_state(const KParams& P, int row, int kind, int token, floa
 
 // Finalize one row from sorted entries e[0, m.n). Returns false when the row must take the
 // exact search.
-__device__ bool finalize_sorted(const KParams& P, const RowCfg& c, int row, const MergeIn& m,
+__device__ __noinline__ bool finalize_sorted(const KParams& P, const RowCfg& c, int row, const MergeIn& m,
                                 const unsigned long long* e, Smem& S) {
   const int tid = threadIdx.x;
   if (m.n == 0) {
@@ -693,7 +608,9 @@ __device__ bool finalize_sorted(const KParams& P, const RowCfg& c, int row, cons
   for (int j = j0; j < j1; ++j) loc += ex2((from_okey(comp_key(e[j])) - mv) * LOG2E);
   float total;
   const float pre = cta_excl_scan_f(loc, &total, S);
-  const float Ssum = c.topk ? total : m.s;
+  float Ssum = c.topk ? total : m.s;
+  // the sums are relative to the largest raw logit; rescale when that one was penalised
+  if (!c.topk && vf(m.m_y, c) != mv) Ssum *= ex2(m.m_y * c.c2 - mv * LOG2E);
   const bool listed_all = c.topk || !more;  // every kept-by-top-k token is among the entries
 
   // first index in [0, lim) whose inclusive prefix C_j satisfies C_j >= t (ge) or C_j > t
@@ -762,14 +679,101 @@ __device__ bool finalize_sorted(const KParams& P, const RowCfg& c, int row, cons
   return true;
 }
 
+// finalize_sorted for short lists (m.n <= 64), by one warp with no CTA barrier: each lane holds
+// entries 2 * lane and 2 * lane + 1; prefix sums are a warp scan. Same decisions as
+// finalize_sorted; called by the 32 lanes of one warp, every lane returns the same value.
+__device__ bool finalize_warp(const KParams& P, const RowCfg& c, int row, const MergeIn& m,
+                              const unsigned long long* e) {
+  const int lane = threadIdx.x & 31;
+  const int n = m.n;
+  const float mv = from_okey(comp_key(e[0]));
+  if (!(mv > -INFINITY) || !(mv <= FLT_MAX)) {
+    if (lane == 0) {
+      write_state(P, row, 3, -1, 0.f, 0.f, 0u, 0);
+      status_or(P, VINFER_ST_NONFINITE);
+    }
+    return true;
+  }
+  const bool more = (m.flags & REC_UNRETAINED) != 0;
+  int nk, avail;
+  if (c.topk) {
+    nk = (n >= c.K) ? count_ge(e, n, comp_key(e[c.K - 1])) : n;
+    avail = nk;
+  } else {
+    avail = more ? count_ge(e, n, m.d_key) : n;
+    nk = 0x7FFFFFFF;
+  }
+  const int j0 = 2 * lane, j1 = j0 + 1;
+  const float v0 = j0 < n ? from_okey(comp_key(e[j0])) : -INFINITY;
+  const float v1 = j1 < n ? from_okey(comp_key(e[j1])) : -INFINITY;
+  const float w0 = j0 < avail ? ex2((v0 - mv) * LOG2E) : 0.f;
+  const float w1 = j1 < avail ? ex2((v1 - mv) * LOG2E) : 0.f;
+  float inc = w0 + w1;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float t = __shfl_up_sync(FULLMASK, inc, o);
+    if (lane >= o) inc += t;
+  }
+  const float C0 = inc - w1, C1 = inc;  // inclusive prefixes at j0 and j1
+  const float total = __shfl_sync(FULLMASK, inc, 31);
+  float Ssum = c.topk ? total : m.s;
+  if (!c.topk && vf(m.m_y, c) != mv) Ssum *= ex2(m.m_y * c.c2 - mv * LOG2E);
+  const bool listed_all = c.topk || !more;
+  // first index whose pair flag is set (lane order, then j0 before j1); -1 when none
+  auto first = [&](bool f0, bool f1) -> int {
+    const unsigned b = __ballot_sync(FULLMASK, f0 || f1);
+    if (!b) return -1;
+    const int l = __ffs(b) - 1;
+    return 2 * l + (__shfl_sync(FULLMASK, f0, l) ? 0 : 1);
+  };
+  int L = 0x7FFFFFFF;
+  if (c.topk) L = nk;
+  else if (!more) L = n;
+  bool cut_beyond = false;
+  if (c.p < 1.f) {  // top-p: keep tokens whose mass strictly before them is < top_p
+    const float t = c.p * Ssum;
+    const int h = first(j0 < avail && C0 >= t, j1 < avail && C1 >= t);
+    if (h >= 0) L = min(L, h + 1);
+    else if (!listed_all) cut_beyond = true;
+  }
+  if (c.minp > 0.f) {  // min-p: keep tokens with exp(v - max) >= min_p
+    const int h = first(j0 < avail && (v0 - mv) * LOG2E < c.lm,
+                        j1 < avail && (v1 - mv) * LOG2E < c.lm);
+    if (h >= 0) L = min(L, max(h, 1));
+    else if (!listed_all) cut_beyond = true;
+  }
+  const bool L_known = L <= avail;
+  if (!L_known && cut_beyond) return false;
+  float s_kept = Ssum;
+  if (L_known) {
+    const int last = L - 1;
+    const float cl = (last & 1) ? C1 : C0;
+    s_kept = __shfl_sync(FULLMASK, cl, last >> 1);
+  }
+  const int lim = L_known ? L : avail;
+  const float t = c.u * s_kept;
+  int j = first(j0 < lim && C0 > t, j1 < lim && C1 > t);
+  if (j < 0) {
+    if (L_known) j = L - 1;
+    else return false;
+  }
+  if (lane == 0) {
+    if (L_known)
+      write_state(P, row, 0, comp_id(e[j]), mv, s_kept, comp_key(e[L - 1]), comp_id(e[L - 1]));
+    else
+      write_state(P, row, 1, comp_id(e[j]), mv, s_kept, 0u, 0);
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------------------------------------
 // exact multi-pass search over one row (global memory), for rows the records cannot resolve
 // ---------------------------------------------------------------------------------------------
-// penalised-position bitmap of a whole row: the candidate buffer's words first, then a stage's
+// penalised-position bitmap of a whole row: the candidate region's words, then scratch's
 struct RowBits {
   uint32_t* w0;
   uint32_t* w1;
-  static constexpr int N0 = RUN_CAP * 2;
+  static constexpr int N0 = CAND_BUF * 2;
   __device__ uint32_t& word(int w) const { return w < N0 ? w0[w] : w1[w - N0]; }
   __device__ bool bit(int i) const { return (word(i >> 5) >> (i & 31)) & 1u; }
 };
@@ -956,8 +960,8 @@ __device__ int exact_jth(const ExactRow<TIn>& X, const Cut& cut, uint32_t w, int
 }
 
 template <typename TIn>
-__device__ void exact_row(const KParams& P, const RowCfg& c, int row, Smem& S,
-                          unsigned char* scratch) {
+__device__ __noinline__ void exact_row(const KParams& P, const RowCfg& c, int row, Smem& S,
+                                       unsigned char* scratch) {
   const int tid = threadIdx.x;
   const RowBits bm{(uint32_t*)S.cand, (uint32_t*)scratch};
   ExactRow<TIn> X{P, c, bm, (const TIn*)P.logits + (int64_t)row * P.ld, 0, 0, (int)P.V, 0.f};
@@ -1095,7 +1099,7 @@ __device__ void exact_row(const KParams& P, const RowCfg& c, int row, Smem& S,
 // finishing a row: local shard record, final answer, or the exact search
 // ---------------------------------------------------------------------------------------------
 template <typename TIn>
-__device__ void finish_row(const KParams& P, Smem& S, unsigned char* scratch, int row,
+__device__ __noinline__ void finish_row(const KParams& P, Smem& S, unsigned char* scratch, int row,
                            const unsigned char* src0, size_t stride, int nsrc, bool local,
                            int* unresolved) {
   const int tid = threadIdx.x;
@@ -1164,103 +1168,10 @@ __device__ __forceinline__ int seg_owner(const KParams& P, int sg) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// producer warp: stages segments for the consumers
-// ---------------------------------------------------------------------------------------------
-template <typename TIn>
-__device__ void producer(const KParams& P, Smem& S) {
-  using E = Elem<TIn>;
-  constexpr int ES = 16 / E::A;
-  const int lane = threadIdx.x & 31;
-  const int s0 = seg_begin(P, blockIdx.x), s1 = seg_begin(P, blockIdx.x + 1);
-  float prm = 0.f;
-  bool pen = false;
-  int64_t hp = 0, hend = 0;
-  for (int i = 0; s0 + i < s1; ++i) {
-    const int sg = s0 + i, row = sg / P.nseg, seg = sg - row * P.nseg;
-    const int s = i % NSTAGE, use = i / NSTAGE;
-    const Geo g = geometry<TIn>(P, row, seg);
-    if (i == 0 || seg == 0) {  // a new run: the row's parameters and history position
-      prm = lane < 8 ? load_param(P, row, lane) : 0.f;
-      const float rep = __shfl_sync(FULLMASK, prm, 3);
-      const float pres = __shfl_sync(FULLMASK, prm, 4);
-      const float freq = __shfl_sync(FULLMASK, prm, 5);
-      pen = P.hrow != nullptr && (rep != 1.f || pres != 0.f || freq != 0.f);
-      if (pen) {
-        const int64_t a = __ldg(P.hrow + row);
-        hend = __ldg(P.hrow + row + 1);
-        // the first entry at or after this segment's first global id (entries of lower
-        // vocabulary shards precede it when the row is sharded)
-        hp = (seg == 0 && P.voff == 0) ? a : warp_lower_bound(P.hids, a, hend, g.gbase, lane);
-      }
-    }
-    // penalised tokens of this segment: the next entries of the row's ascending history
-    int ns = 0;
-    int rid[SIDE_PER_LANE], rcn[SIDE_PER_LANE];
-    if (pen) {
-      const int64_t lim = g.gbase + g.n;
-#pragma unroll
-      for (int q = 0; q < SIDE_PER_LANE; ++q) {
-        const int64_t p = hp + lane + 32 * q;
-        rid[q] = p < hend ? __ldg(P.hids + p) : 0x7FFFFFFF;
-        rcn[q] = p < hend ? __ldg(P.hcnt + p) : 0;
-      }
-#pragma unroll
-      for (int q = 0; q < SIDE_PER_LANE; ++q)
-        ns += __popc(__ballot_sync(FULLMASK, (int64_t)rid[q] < lim));
-      if (ns == SIDE_CAP) {  // the window is full: find the end of this segment's entries
-        const int64_t e = warp_lower_bound(P.hids, hp + SIDE_CAP, hend, lim, lane);
-        if (e > hp + SIDE_CAP) {
-          hp = e;
-          ns = -1;  // more penalised tokens than a stage holds: the row takes the exact search
-        } else {
-          hp += SIDE_CAP;
-        }
-      } else {
-        hp += ns;
-      }
-    }
-    uint32_t hv = 0, tv = 0;
-    if (lane < g.head) hv = E::ldraw(g.rowp, g.lo + lane);
-    if (lane < g.n - g.tail0) tv = E::ldraw(g.rowp, g.lo + g.tail0 + lane);
-    // ---- wait until the consumers released this stage's previous segment
-    if (use >= 1 && !mbar_wait_bounded(&S.empty[s], (use - 1) & 1)) {
-      if (lane == 0) status_or(P, VINFER_ST_TIMEOUT);
-      return;
-    }
-    Stage& st = S.st[s];
-    if (lane < 8) st.prm[lane] = prm;
-    if (lane == 0) st.ns = ns;
-#pragma unroll
-    for (int q = 0; q < SIDE_PER_LANE; ++q) {
-      const int j = lane + 32 * q;
-      if (j < ns) {
-        st.side_id[j] = rid[q];
-        st.side_cnt[j] = rcn[q];
-      }
-    }
-    if (lane < g.off) E::neg_inf(st.data, lane);
-    if (lane < g.pad_end) E::neg_inf(st.data, g.off + g.n + lane);
-    if (lane < g.head) E::straw(st.data, g.off + lane, hv);
-    if (lane < g.n - g.tail0) E::straw(st.data, g.off + g.tail0 + lane, tv);
-    __syncwarp();
-    if (lane == 0) {
-      const uint32_t bytes = (uint32_t)g.inter * ES;
-      mbar_arrive_expect_tx(&S.full[s], bytes);
-      for (uint32_t b = 0; b < bytes; b += 16384u) {
-        tma_load_1d(st.data + (size_t)(g.off + g.head) * ES + b,
-                    (const unsigned char*)((const TIn*)g.rowp + g.lo + g.head) + b,
-                    min(16384u, bytes - b), &S.full[s]);
-      }
-    }
-    __syncwarp();
-  }
-}
-
-// ---------------------------------------------------------------------------------------------
-// consumers
+// streaming: each CTA streams its segments with plain 16-byte loads held in registers
 // ---------------------------------------------------------------------------------------------
 // smallest y with vf(y) >= vt: about y = vt * T; the boundary lies within a few keys of it in
-// the normal range, found by one round of 32 probes (a full binary search otherwise)
+// the normal range, found by one round of 32 probes (a full binary search otherwise). Warp-wide.
 __device__ float ylo_for(float vt, const RowCfg& c) {
   if (c.greedy || vt == -INFINITY) return vt;
   const int lane = threadIdx.x & 31;
@@ -1282,449 +1193,825 @@ __device__ float ylo_for(float vt, const RowCfg& c) {
   return from_okey(hi);
 }
 
-// append a candidate to the run's buffer (overflow is flagged, never written past the end)
-__device__ __forceinline__ void add_cand(Smem& S, unsigned long long e) {
-  const int pos = atomicAdd(&S.sc[SC_NC], 1);
-  if (pos < RUN_CAP) S.cand[pos] = e;
-}
-
-// Sorts the run's candidates and keeps the K largest with every tie of the K-th: the kept
-// entries land sorted in out[0, n_ret). Returns n_ret; *tkey receives the K-th key (0 when all
-// n candidates are kept because n < K). The candidates stay untouched.
-__device__ int select_sorted(Smem& S, int n, int K, unsigned long long* out, uint32_t* tkey) {
+// Sorts buf[0, n) in place (n <= CAND_BUF) and keeps the K largest with every tie of the K-th
+// at the front. Returns the kept count; *tkey receives the K-th key (0 when n < K).
+__device__ int select_inplace(unsigned long long* buf, int n, int K, uint32_t* tkey, Smem& S) {
   const int tid = threadIdx.x;
   if (n <= NT) {  // rank by counting: one candidate per thread
     unsigned long long x = 0ull;
     int rank = 0;
     if (tid < n) {
-      x = S.cand[tid];
-      for (int j = 0; j < n; ++j) rank += S.cand[j] < x;
+      x = buf[tid];
+#pragma unroll 8
+      for (int j = 0; j < n; ++j) rank += buf[j] < x;
       if (rank == K - 1) S.sc[SC_TKEY] = (int)comp_key(x);
     }
-    cbar();
-    const uint32_t t = n >= K ? (uint32_t)S.sc[SC_TKEY] : 0u;
     if (tid == 0) S.sc[SC_NRET] = 0;
     cbar();
+    const uint32_t t = n >= K ? (uint32_t)S.sc[SC_TKEY] : 0u;
     if (tid < n && comp_key(x) >= t) {
-      out[rank] = x;
+      buf[rank] = x;
       atomicMax(&S.sc[SC_NRET], rank + 1);
     }
     cbar();
     *tkey = t;
-    return S.sc[SC_NRET];
+    const int r = S.sc[SC_NRET];
+    cbar();
+    return r;
   }
-  // larger sets (rare): bitonic sort of a padded copy, then cut at the K-th
+  // larger sets (rare): bitonic sort, padded to a power of two with the largest key
   int np = 1;
   while (np < n) np <<= 1;
-  for (int j = tid; j < np; j += NT) out[j] = j < n ? S.cand[j] : ~0ull;
+  for (int j = n + tid; j < np; j += NT) buf[j] = ~0ull;
   cbar();
   for (int k = 2; k <= np; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
       for (int i = tid; i < np; i += NT) {
         const int ixj = i ^ j;
         if (ixj > i) {
-          const unsigned long long a = out[i], b = out[ixj];
+          const unsigned long long a = buf[i], b = buf[ixj];
           if ((a > b) == ((i & k) == 0)) {
-            out[i] = b;
-            out[ixj] = a;
+            buf[i] = b;
+            buf[ixj] = a;
           }
         }
       }
       cbar();
     }
   }
-  const uint32_t t = n >= K ? comp_key(out[K - 1]) : 0u;
+  const uint32_t t = n >= K ? comp_key(buf[K - 1]) : 0u;
   *tkey = t;
-  return n >= K ? count_ge(out, n, t) : n;
+  return n >= K ? count_ge(buf, n, t) : n;
 }
 
-// the elements of one staged vector at or above ylo become candidates
-template <typename TIn>
-__device__ __noinline__ void expand_vector(Smem& S, const RowCfg& c, const Geo& g, uint4 q, int j,
-                                           float ylo, bool checkbits) {
-  using E = Elem<TIn>;
-#pragma unroll 1
-  for (int e = 0; e < E::A; ++e) {
-    const int slot = j * E::A + e;
-    const int li = slot - g.off;
-    if (li < 0 || li >= g.n) continue;
-    if (checkbits && ((S.bitmap[slot >> 5] >> (slot & 31)) & 1u)) continue;
-    const float y = E::at(q, e);
-    if (y >= ylo) add_cand(S, comp(okey(vf(y, c)), (int)(g.gbase + li)));
+// the run's view of the row's history: the entries whose ids fall inside the run, in shared
+// memory (ids, then counts) when they fit, else read from global memory
+struct RunHist {
+  const int* ids;
+  const int* cnt;
+  int n;
+  bool shared;
+};
+// the run's history view, as run() staged it (Smem::hpos, SC_NH, the table in scratch)
+__device__ __forceinline__ RunHist hist_view(const KParams& P, Smem& S) {
+  RunHist h;
+  h.n = S.sc[SC_NH];
+  h.shared = h.n <= HIST_CAP;
+  if (h.shared) {
+    h.ids = reinterpret_cast<const int*>(S.scratch);
+    h.cnt = h.ids + HIST_CAP;
+  } else {
+    h.ids = P.hids + S.hpos;
+    h.cnt = P.hcnt + S.hpos;
   }
+  return h;
+}
+__device__ __forceinline__ int hist_count(const RunHist& h, int id) {
+  int a = 0, b = h.n;
+  while (a < b) {
+    const int mid = (a + b) >> 1;
+    const int v = h.shared ? h.ids[mid] : __ldg(h.ids + mid);
+    if (v < id) a = mid + 1; else b = mid;
+  }
+  if (a >= h.n) return 0;
+  const int v = h.shared ? h.ids[a] : __ldg(h.ids + a);
+  if (v != id) return 0;
+  return h.shared ? h.cnt[a] : __ldg(h.cnt + a);
 }
 
-struct RunState {        // per consumer thread, carried across the segments of a run
-  float m_t, s_t;        // online softmax max and sum (top-k off)
-  unsigned long long gbest;  // greedy: smallest composite key (max value, first index)
+// ---- delegates --------------------------------------------------------------------------------
+// While streaming, a vector (or an edge element) whose maximum reaches the threshold is only
+// noted: its maximum raw logit and the id of its first element. At the end of the run the K-th
+// largest delegate bounds the run's K-th largest value closely, and only the vectors at or above
+// that bound are read again and expanded. Entry: (~okey(max) << 32) | flags | first id, so
+// ascending entries are descending maxima.
+constexpr uint32_t DL_PEN = 0x80000000u;  // a history id falls inside: the max may be penalised
+constexpr uint32_t DL_ONE = 0x40000000u;  // an edge element, not a 16-byte vector
+constexpr uint32_t DL_ID = 0x3FFFFFFFu;
+static_assert(2 * (int64_t)VINFER_MAX_VOCAB <= (int64_t)DL_ID, "global ids fit a delegate");
+
+__device__ __forceinline__ unsigned long long dele(float vmax, uint32_t bits) {
+  return ((unsigned long long)(~okey(vmax)) << 32) | bits;
+}
+__device__ __forceinline__ float dele_max(unsigned long long d) {
+  return from_okey(~(uint32_t)(d >> 32));
+}
+
+// does an id of the run's history fall in [id0, id0 + n)?
+__device__ __forceinline__ bool hist_any(const RunHist& h, int id0, int n) {
+  int a = 0, b = h.n;
+  while (a < b) {
+    const int mid = (a + b) >> 1;
+    const int v = h.shared ? h.ids[mid] : __ldg(h.ids + mid);
+    if (v < id0) a = mid + 1; else b = mid;
+  }
+  if (a >= h.n) return false;
+  const int v = h.shared ? h.ids[a] : __ldg(h.ids + a);
+  return v < id0 + n;
+}
+
+// Note one delegate in the run's list (any lane). Returns its slot; slots past the list are
+// counted, not written (the run then takes the exact search).
+__device__ __forceinline__ int dele_push(Smem& S, unsigned long long d) {
+  const int pos = atomicAdd(&S.sc[SC_NC], 1);
+  if (pos < CAND_BUF) S.cand[pos] = d;
+  return pos;
+}
+
+constexpr int TB = 64;  // the list is tightened once per block of TB delegates
+
+// A list entry once its writer has stored it (the list starts filled with ~0); gives up after a
+// bounded number of polls and reports the entry as absent, which only weakens the bound.
+__device__ __forceinline__ unsigned long long list_entry(const Smem& S, int i) {
+  const volatile unsigned long long* v = S.cand;
+  unsigned long long x = v[i];
+  for (int it = 0; x == ~0ull && it < 4096; ++it) x = v[i];
+  return x;
+}
+
+// The warp that completed block [b0, b0 + TB) of the list raises the CTA's threshold to the
+// K-th largest unflagged delegate of that block (K distinct vectors without history ids reach
+// it). Warp-wide; K <= TB.
+__device__ __forceinline__ void block_tighten(const KParams& P, int b0, int K, float T, bool greedy,
+                                           bool pen, int vec_len, Smem& S) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long v0 = list_entry(S, b0 + lane), v1 = list_entry(S, b0 + 32 + lane);
+  if (pen) {  // delegates holding a history id are not counted
+    const RunHist h = hist_view(P, S);
+    if (v0 != ~0ull && hist_any(h, (int)((uint32_t)v0 & DL_ID), ((uint32_t)v0 & DL_ONE) ? 1 : vec_len))
+      v0 = ~0ull;
+    if (v1 != ~0ull && hist_any(h, (int)((uint32_t)v1 & DL_ID), ((uint32_t)v1 & DL_ONE) ? 1 : vec_len))
+      v1 = ~0ull;
+  }
+  int r0 = 0, r1 = 0;
+#pragma unroll 4
+  for (int k = 0; k < 32; ++k) {
+    const unsigned long long a = __shfl_sync(FULLMASK, v0, k), b = __shfl_sync(FULLMASK, v1, k);
+    r0 += (a < v0) + (b < v0);
+    r1 += (a < v1) + (b < v1);
+  }
+  unsigned long long kth = ~0ull;
+  if (v0 != ~0ull && r0 == K - 1) kth = v0;
+  if (v1 != ~0ull && r1 == K - 1) kth = v1;
+  const unsigned have = __ballot_sync(FULLMASK, kth != ~0ull);
+  if (!have) return;
+  kth = __shfl_sync(FULLMASK, kth, __ffs(have) - 1);
+  RowCfg c{};
+  c.T = T;
+  c.greedy = greedy;
+  const float y = ylo_for(vf(dele_max(kth), c), c);
+  if (lane == 0) atomicMax(&S.ylo_key, okey(y));
+}
+
+// one segment's loads for this thread: U coalesced vectors and at most one edge scalar
+template <typename TIn>
+struct SegLoad {
+  uint4 q[U];
+  float sy;       // edge scalar (ragged head or tail), -inf when none
+  int64_t sid;    // its global id, -1 when none
+  int64_t gid0;   // global id of the first element of the segment's first vector
+  const uint4* vb;  // the segment's first vector in global memory
+  int nvec;       // vectors in the segment
 };
 
-// One segment of the current run: penalties, then either the running greedy minimum, or the
-// candidates at or above the run's threshold (established on the run's first segment).
 template <typename TIn>
-__device__ void run_segment(const KParams& P, const RowCfg& c, const Geo& g, Stage& st, Smem& S,
-                            RunState& R) {
+__device__ __forceinline__ void load_segment(const KParams& P, const TIn* rowp, int seg,
+                                             SegLoad<TIn>& L) {
   using E = Elem<TIn>;
   constexpr int A = E::A;
-  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  void* sv = st.data;
-  const int ns = st.ns;
-  if (ns < 0) {
-    if (tid == 0) S.sc[SC_RFL] |= RUN_OVER;
-    cbar();
-    return;
-  }
-  // ---- penalised tokens: exact float32 values on the side, -inf in the staged copy
-  if (ns > 0) {
-    const int nwords = (g.nvec * A + 31) / 32;
-    for (int wd = tid; wd < nwords; wd += NT) S.bitmap[wd] = 0u;
-    cbar();
-    for (int j = tid; j < ns; j += NT) {
-      const int cnt = st.side_cnt[j];
-      const int64_t li = (int64_t)st.side_id[j] - g.gbase;
-      const int slot = g.off + (int)li;
-      const bool inside = li >= 0 && li < g.n;  // false only for a history out of order
-      if (!inside) status_or(P, VINFER_ST_INTERNAL);
-      if (cnt > 0 && inside) {
-        S.side_y[j] = penalize(E::sm(sv, slot), cnt, c);
-        atomicOr(&S.bitmap[slot >> 5], 1u << (slot & 31));
-        E::neg_inf(sv, slot);
-      } else {
-        S.side_y[j] = __int_as_float(0x7fc00000);  // NaN: not penalised, value stays in place
-      }
-    }
-    cbar();
-  }
-  const uint4* sv4 = (const uint4*)sv;
-  if (c.greedy) {  // running first argmax
-    float best = R.gbest == ~0ull ? -INFINITY : from_okey(comp_key(R.gbest));
-    for (int j = tid; j < g.nvec; j += NT) {
-      const uint4 q = sv4[j];
-      const float vm = E::vmax(q);
-      if (vm > best) {
-        int e = 0;
-        while (e < A - 1 && E::at(q, e) != vm) ++e;
-        const unsigned long long cc = comp(okey(vm), (int)(g.gbase + j * A + e - g.off));
-        R.gbest = cc < R.gbest ? cc : R.gbest;
-        best = vm;
-      }
-    }
-    for (int j = tid; j < ns; j += NT) {
-      const float y = S.side_y[j];
-      if (isnan(y)) continue;
-      const unsigned long long cc = comp(okey(y), st.side_id[j]);
-      R.gbest = cc < R.gbest ? cc : R.gbest;
-    }
-    cbar();
-    return;
-  }
-  const float ylo0 = S.sf[SF_YLO];
-  const bool known = !isnan(ylo0);  // the run's collection threshold exists
-  const bool checkbits = ns > 0;    // penalised slots hold -inf; only a -inf bound reaches them
-  float ylo = ylo0;
-  if (known) {
-    // ---- stream: each vector's maximum against the threshold; the rare vector that reaches
-    //      it is expanded in place by the thread that read it
-    for (int j = tid; j < g.nvec; j += NT) {
-      const uint4 q = sv4[j];
-      const float vm = E::vmax(q);
-      if (c.need_sum) {
-        if (vm > R.m_t) {
-          R.s_t *= ex2((R.m_t - vm) * c.c2);
-          R.m_t = vm;
-        }
+  constexpr int ES = 16 / A;
+  const int tid = threadIdx.x;
+  const int64_t lo = (int64_t)seg * P.seg_len;
+  const int n = (int)(min(P.V, lo + (int64_t)P.seg_len) - lo);
+  const uintptr_t gaddr = (uintptr_t)(rowp + lo);
+  int head = (int)(((16u - (uint32_t)(gaddr & 15u)) & 15u) / ES);
+  if (head > n) head = n;
+  L.nvec = (int)(((int64_t)(n - head) * ES) / 16);
+  const int tail0 = head + L.nvec * A;
+  const uint4* vb = reinterpret_cast<const uint4*>(rowp + lo + head);
+  L.vb = vb;
+  L.gid0 = P.voff + lo + head;
 #pragma unroll
-        for (int e = 0; e < A; ++e) R.s_t += ex2((E::at(q, e) - R.m_t) * c.c2);
-      }
-      if (vm >= ylo) expand_vector<TIn>(S, c, g, q, j, ylo, checkbits && ylo == -INFINITY);
-    }
-    for (int j = tid; j < ns; j += NT) {
-      const float y = S.side_y[j];
-      if (isnan(y)) continue;
-      if (c.need_sum) {
-        if (y > R.m_t) {
-          R.s_t *= ex2((R.m_t - y) * c.c2);
-          R.m_t = y;
-        }
-        R.s_t += ex2((y - R.m_t) * c.c2);
-      }
-      if (y >= ylo) add_cand(S, comp(okey(vf(y, c)), st.side_id[j]));
-    }
-  } else {
-    // ---- first segment of the run: per-thread maxima, then a bound on the K-th largest
-    float tmax = -INFINITY;
-    for (int j = tid; j < g.nvec; j += NT) {
-      const uint4 q = sv4[j];
-      const float vm = E::vmax(q);
-      tmax = fmaxf(tmax, vm);
-      if (c.need_sum) {
-        if (vm > R.m_t) {
-          R.s_t *= ex2((R.m_t - vm) * c.c2);
-          R.m_t = vm;
-        }
-#pragma unroll
-        for (int e = 0; e < A; ++e) R.s_t += ex2((E::at(q, e) - R.m_t) * c.c2);
-      }
-    }
-    for (int j = tid; j < ns; j += NT) {
-      const float y = S.side_y[j];
-      if (isnan(y)) continue;
-      tmax = fmaxf(tmax, y);
-      if (c.need_sum) {
-        if (y > R.m_t) {
-          R.s_t *= ex2((R.m_t - y) * c.c2);
-          R.m_t = y;
-        }
-        R.s_t += ex2((y - R.m_t) * c.c2);
-      }
-    }
-    // each warp extracts its kw = ceil(K / 8) largest lane maxima (distinct elements); the
-    // K-th largest of those 8 * kw values bounds the segment's K-th largest value from below
-    const int kw = min((c.K + NCW - 1) / NCW, 32);
-    {
-      float mine = tmax;
-      for (int r = 0; r < kw; ++r) {
-        float m = mine;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(FULLMASK, m, o));
-        const unsigned b = __ballot_sync(FULLMASK, mine == m && m > -INFINITY);
-        if (lane == 0) S.ext[w * 32 + r] = b ? m : -INFINITY;
-        if (b && lane == __ffs(b) - 1) mine = -INFINITY;
-      }
-    }
-    if (tid == 0) S.sf[SF_TH] = -INFINITY;  // fewer than K finite values: no bound
-    cbar();
-    if (tid < NCW * kw) {
-      // rank of this value in the union of the eight descending lists (ties by list index)
-      const int wl = tid / kw, r = tid - wl * kw;
-      const float x = S.ext[wl * 32 + r];
-      int rank = r;
-      for (int o = 0; o < NCW; ++o) {
-        if (o == wl) continue;
-        const float* L = S.ext + o * 32;
-        int a = 0, b = kw;
-        while (a < b) {
-          const int mid = (a + b) >> 1;
-          if (o < wl ? (L[mid] >= x) : (L[mid] > x)) a = mid + 1; else b = mid;
-        }
-        rank += a;
-      }
-      if (rank == c.K - 1 && x > -INFINITY) S.sf[SF_TH] = x;
-    }
-    cbar();
-    if (w == 0) {
-      const float th = S.sf[SF_TH];
-      const float y = th == -INFINITY ? -INFINITY : ylo_for(vf(th, c), c);
-      if (lane == 0) S.sf[SF_YLO] = y;
-    }
-    cbar();
-    ylo = S.sf[SF_YLO];
-    for (int j = tid; j < g.nvec; j += NT) {
-      const uint4 q = sv4[j];
-      if (E::vmax(q) >= ylo) expand_vector<TIn>(S, c, g, q, j, ylo, checkbits && ylo == -INFINITY);
-    }
-    for (int j = tid; j < ns; j += NT) {
-      const float y = S.side_y[j];
-      if (y >= ylo) add_cand(S, comp(okey(vf(y, c)), st.side_id[j]));
-    }
+  for (int u = 0; u < U; ++u) {
+    const int j = tid + NT * u;
+    L.q[u] = j < L.nvec ? __ldg(vb + j) : make_uint4(0u, 0u, 0u, 0u);
   }
-  cbar();
-  const int nc = S.sc[SC_NC];
-  if (nc > RUN_CAP) {
-    if (tid == 0) S.sc[SC_RFL] |= RUN_OVER;
-    cbar();
-    return;
+  L.sid = -1;
+  L.sy = -INFINITY;
+  if (tid < head) {
+    L.sid = lo + tid;
+  } else if (tid >= 32 && tid - 32 < n - tail0) {
+    L.sid = lo + tail0 + (tid - 32);
   }
-  // ---- tighten: whenever the buffer holds more than max(2K, 64) candidates (and after the
-  //      run's first segment), keep only the K largest (with ties) and raise the threshold to
-  //      the K-th value, so later segments contribute fewer candidates
-  if ((!known && nc > c.K) || nc > max(2 * c.K, 64)) {
-    unsigned long long* tmp = (unsigned long long*)st.data;  // the segment is done with
-    uint32_t t;
-    const int nr = select_sorted(S, nc, c.K, tmp, &t);
-    for (int j = tid; j < nr; j += NT) S.cand[j] = tmp[j];
-    if (tid == 0) S.sc[SC_NC] = nr;
-    if (w == 0) {
-      const float y = ylo_for(from_okey(t), c);
-      if (lane == 0) S.sf[SF_YLO] = y;
-    }
-    cbar();
+  if (L.sid >= 0) {
+    L.sy = E::ld(rowp, L.sid);
+    L.sid += P.voff;
   }
 }
 
-// Completes the run: its sorted candidates become the row's answer (single-run rows), a shard
-// record (local mode), or a run record for the CTA that completes the row last to merge.
+// The run's first threshold, from its first segment (CTA-wide, once per run): each warp sorts
+// its lanes' largest vector maxima (a bitonic sort of (value, vector) pairs) and publishes its
+// kk = min(K, 32) best, leaving out vectors that hold a history id (their maximum may be a
+// penalised token); the K-th largest of the 8 * kk published values is reached by K distinct
+// vectors, so it bounds the run's K-th largest processed value from below.
 template <typename TIn>
-__device__ void run_end(const KParams& P, const RowCfg& c, int row, int first_seg, int last_seg,
-                        Smem& S, RunState& R, unsigned char* scratch) {
-  const int tid = threadIdx.x;
-  const int nruns = seg_owner(P, row * P.nseg + P.nseg - 1) - seg_owner(P, row * P.nseg) + 1;
-  const int run_idx = blockIdx.x - seg_owner(P, row * P.nseg);
-  const int64_t lo = (int64_t)first_seg * P.seg_len;
-  const int64_t hi = min(P.V, (int64_t)(last_seg + 1) * P.seg_len);
-  const int n_run = (int)(hi - lo);
-  unsigned long long* sorted = (unsigned long long*)scratch;
-  // the run's own record, in shared memory first
-  uint32_t flags = 0, tkey = 0;
-  int nret = 0;
-  float m_y = -INFINITY, s_run = 0.f;
-  if (c.bad) {
-    flags = REC_BAD;
-  } else if (c.exact || (S.sc[SC_RFL] & RUN_OVER)) {
-    flags = c.exact ? REC_EXACT : REC_OVERFLOW;
-  } else if (c.greedy) {
-    const unsigned long long b = cta_min_u64(R.gbest, S);
-    if (b != ~0ull) {
-      sorted[0] = b;
-      nret = 1;
-      m_y = from_okey(comp_key(b));
-      tkey = comp_key(b);
+__device__ __forceinline__ void cta_first_bound(const KParams& P, const SegLoad<TIn>& L,
+                                                const float* vm, int K, float T, bool greedy,
+                                                bool pen, Smem& S) {
+  constexpr int A = Elem<TIn>::A;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  float lv = -INFINITY;
+  int lid = -1;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if (vm[u] > lv) {
+      lv = vm[u];
+      lid = (int)(L.gid0 + (int64_t)(tid + NT * u) * A);
     }
-    if (n_run > 1) flags = REC_UNRETAINED;
-  } else {
-    const int nc = S.sc[SC_NC];
-    nret = select_sorted(S, nc, c.K, sorted, &tkey);
-    if (nret > CAND_CAP) flags = REC_OVERFLOW;
-    else if (nret < n_run) flags = REC_UNRETAINED;
-    else tkey = 0u;
-    if (c.need_sum) {  // rescale every partial sum to the run maximum, fixed order
-      const uint32_t mk = cta_max_u32(okey(R.m_t == -FLT_MAX ? -INFINITY : R.m_t), S);
-      m_y = from_okey(mk);
-      const float part = (R.m_t == -FLT_MAX) ? 0.f : R.s_t * ex2((R.m_t - m_y) * c.c2);
-      float tot;
-      cta_excl_scan_f(part, &tot, S);
-      s_run = tot;
+  }
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {  // descending bitonic sort of the pairs
+#pragma unroll
+    for (int jj = k >> 1; jj > 0; jj >>= 1) {
+      const float ov = __shfl_xor_sync(FULLMASK, lv, jj);
+      const int oid = __shfl_xor_sync(FULLMASK, lid, jj);
+      const bool take_max = ((lane & jj) == 0) == ((lane & k) == 0);
+      if (take_max ? (ov > lv) : (ov < lv)) {
+        lv = ov;
+        lid = oid;
+      }
+    }
+  }
+  const int kk = min(K, 32);
+  if (lane < kk) {
+    float v = lv;
+    if (pen && lid >= 0 && hist_any(hist_view(P, S), lid, A)) v = -INFINITY;
+    S.ext[w * 32 + lane] = v;
+  }
+  if (tid == 0) S.sf[SF_TH] = -INFINITY;  // fewer than K usable values: no bound
+  cbar();
+  if (lane < kk) {
+    const float x = S.ext[tid];
+    int rank = 0;
+    for (int o = 0; o < NCW; ++o) {
+#pragma unroll 8
+      for (int r = 0; r < kk; ++r) {
+        const float z = S.ext[o * 32 + r];
+        rank += (z > x) || (z == x && o * 32 + r < tid);
+      }
+    }
+    if (rank == K - 1 && x > -INFINITY) S.sf[SF_TH] = x;
+  }
+  cbar();
+  if (w == 0) {
+    const float th = S.sf[SF_TH];
+    if (th > -INFINITY) {
+      RowCfg c{};
+      c.T = T;
+      c.greedy = greedy;
+      const float y = ylo_for(vf(th, c), c);
+      if (lane == 0) atomicMax(&S.ylo_key, okey(y));
     }
   }
   cbar();
-  if (nruns == 1 && P.mode == 0) {  // the whole row is here: answer it directly
-    if (flags & REC_BAD) {
-      if (tid == 0) {
+}
+
+// ---------------------------------------------------------------------------------------------
+// k_stream: every row streamed once; each run leaves an unsorted candidate record
+// ---------------------------------------------------------------------------------------------
+// A run record (global workspace, one slot per row and run): the run's threshold on raw logits,
+// its delegates (unsorted; every vector of the run holding a non-penalised element at or above
+// the threshold has one), and for rows without top-k its maximum raw logit and the softmax sum
+// of its raw logits relative to it. Greedy rows without penalties keep one entry instead: the
+// run's smallest composite key.
+struct RunRec {
+  float m;           // largest raw logit of the run (rows without top-k)
+  float s;           // sum of exp2((y - m) * log2(e) / T) over the run's raw logits
+  uint32_t ylo_key;  // ordered key of the run's threshold on raw logits
+  int32_t n;         // entries
+  uint32_t flags;    // REC_*
+  int32_t pad[3];
+};
+static_assert(sizeof(RunRec) == 32, "run record header is 32 bytes");
+
+enum { MODE_GREEDY = 0, MODE_CANDS = 1, MODE_CANDS_SUM = 2 };
+
+// The streaming loop of one run, specialised per kind of row so each variant keeps only its
+// own state in registers: MODE 0 greedy (first index of the maximum), 1 candidates, 2
+// candidates plus the online softmax sum of rows without top-k.
+template <typename TIn, int MODE>
+__device__ __forceinline__ void stream_run(const KParams& P, Smem& S, int row, int seg_a,
+                                           int seg_b, int K, float T, float c2, bool greedy,
+                                           bool pen, SegLoad<TIn>& sa, float& m_t, float& s_t,
+                                           unsigned long long& gbest) {
+  using E = Elem<TIn>;
+  constexpr int A = E::A;
+  const int tid = threadIdx.x;
+  const TIn* rowp = (const TIn*)P.logits + (int64_t)row * P.ld;
+  float bestv = -INFINITY;
+  auto process = [&](const SegLoad<TIn>& L, int seg) {
+    float vm[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) vm[u] = (tid + NT * u < L.nvec) ? E::vmax(L.q[u]) : -INFINITY;
+    if (MODE == MODE_CANDS_SUM) {  // online softmax sum over raw logits (corrected later)
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (tid + NT * u >= L.nvec) continue;
+        if (vm[u] > m_t) {
+          s_t *= ex2((m_t - vm[u]) * c2);
+          m_t = vm[u];
+        }
+#pragma unroll
+        for (int e = 0; e < A; ++e) s_t += ex2((E::at(L.q[u], e) - m_t) * c2);
+      }
+      if (L.sid >= 0) {
+        if (L.sy > m_t) {
+          s_t *= ex2((m_t - L.sy) * c2);
+          m_t = L.sy;
+        }
+        s_t += ex2((L.sy - m_t) * c2);
+      }
+    }
+    if (MODE == MODE_GREEDY) {  // first index of the maximum
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (vm[u] > bestv) {
+          int e = 0;
+          while (e < A - 1 && E::at(L.q[u], e) != vm[u]) ++e;
+          const unsigned long long cc =
+              comp(okey(vm[u]), (int)(L.gid0 + (int64_t)(tid + NT * u) * A + e));
+          gbest = cc < gbest ? cc : gbest;
+          bestv = vm[u];
+        }
+      }
+      if (L.sid >= 0) {
+        const unsigned long long cc = comp(okey(L.sy), (int)L.sid);
+        gbest = cc < gbest ? cc : gbest;
+      }
+      return;
+    }
+    if (seg == seg_a) cta_first_bound<TIn>(P, L, vm, K, T, greedy, pen, S);
+    // the CTA's threshold as it stands: warps raise it as they go
+    const float ylo = from_okey(*reinterpret_cast<volatile uint32_t*>(&S.ylo_key));
+    int trig = -1;  // a block of the list this thread completed
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (tid + NT * u < L.nvec && vm[u] >= ylo) {  // rare
+        const int id0 = (int)(L.gid0 + (int64_t)(tid + NT * u) * A);
+        const int pos = dele_push(S, dele(vm[u], (uint32_t)id0));
+        if (pos % TB == TB - 1 && pos < CAND_BUF) trig = pos - (TB - 1);
+      }
+    }
+    if (L.sid >= 0 && L.sy >= ylo) {
+      const int pos = dele_push(S, dele(L.sy, DL_ONE | (uint32_t)L.sid));
+      if (pos % TB == TB - 1 && pos < CAND_BUF) trig = pos - (TB - 1);
+    }
+    unsigned tb = __ballot_sync(FULLMASK, trig >= 0);
+    while (tb) {  // rare: this warp completed a block of delegates
+      const int src = __ffs(tb) - 1;
+      tb &= tb - 1;
+      block_tighten(P, __shfl_sync(FULLMASK, trig, src), K, T, greedy, pen, A, S);
+    }
+  };
+  // one segment in flight per CTA: the other resident CTAs of the SM keep loads outstanding
+  // while this one processes (a second register buffer would not fit three CTAs per SM)
+  for (int seg = seg_a; seg <= seg_b; ++seg) {
+    if (seg > seg_a) load_segment<TIn>(P, rowp, seg, sa);  // the first was issued by run()
+    process(sa, seg);
+  }
+}
+
+// One run: segments seg_a..seg_b of `row`, streamed by the whole CTA, leaving its record.
+template <typename TIn>
+__device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_a, int seg_b) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  // the loop keeps only these scalars of the row's configuration
+  bool greedy, pen, need_sum, active;
+  float T, c2;
+  int K;
+  uint32_t flags;
+  {
+    const RowCfg c = load_row(P, row);
+    greedy = c.greedy;
+    pen = c.pen;
+    need_sum = c.need_sum;
+    active = !(c.bad || c.exact);
+    flags = c.bad ? REC_BAD : (c.exact ? REC_EXACT : 0u);
+    T = c.T;
+    c2 = c.c2;
+    K = c.greedy ? 1 : c.K;
+  }
+  const bool cands = !greedy || pen;  // greedy with penalties runs as top-1 candidates
+  const int run_idx = blockIdx.x - seg_owner(P, row * P.nseg);
+  unsigned char* rec = P.recs + ((size_t)row * P.nseg + run_idx) * REC_STRIDE;
+  RunRec* hd = reinterpret_cast<RunRec*>(rec);
+  unsigned long long* ent = reinterpret_cast<unsigned long long*>(rec + sizeof(RunRec));
+  // the first segment's loads go out before the set-up below, which they overlap
+  SegLoad<TIn> first;
+  if (active) load_segment<TIn>(P, (const TIn*)P.logits + (int64_t)row * P.ld, seg_a, first);
+  // ---- the history entries inside this run's ids, staged in shared memory
+  if (tid == 0) S.sc[SC_NH] = 0;
+  if (pen && active) {
+    if (tid < 32) {
+      const int64_t a = __ldg(P.hrow + row), b = __ldg(P.hrow + row + 1);
+      const int64_t ia = warp_lower_bound(P.hids, a, b, P.voff + (int64_t)seg_a * P.seg_len, lane);
+      const int64_t ib = warp_lower_bound(
+          P.hids, ia, b, P.voff + min(P.V, (int64_t)(seg_b + 1) * P.seg_len), lane);
+      if (lane == 0) {
+        S.hpos = ia;
+        S.sc[SC_NH] = (int)(ib - ia);
+      }
+    }
+    cbar();
+    const int64_t ia = S.hpos;
+    const int nh = S.sc[SC_NH];
+    if (nh <= HIST_CAP) {
+      int* hid = reinterpret_cast<int*>(S.scratch);
+      for (int j = tid; j < nh; j += NT) {
+        hid[j] = __ldg(P.hids + ia + j);
+        hid[HIST_CAP + j] = __ldg(P.hcnt + ia + j);
+      }
+    }
+  }
+  if (tid == 0) {
+    S.sc[SC_RFL] = 0;
+    S.sc[SC_NC] = 0;
+    S.ylo_key = okey(-INFINITY);
+    S.dkth = ~0ull;
+  }
+  for (int i = tid; i < CAND_BUF; i += NT) S.cand[i] = ~0ull;
+  float m_t = -FLT_MAX, s_t = 0.f;
+  unsigned long long gbest = ~0ull;
+  cbar();
+  if (!active) {
+    if (tid == 0) {
+      hd->m = -INFINITY;
+      hd->s = 0.f;
+      hd->ylo_key = 0u;
+      hd->n = 0;
+      hd->flags = flags;
+    }
+    return;
+  }
+  if (!cands)
+    stream_run<TIn, MODE_GREEDY>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first, m_t,
+                                 s_t, gbest);
+  else if (need_sum)
+    stream_run<TIn, MODE_CANDS_SUM>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first,
+                                    m_t, s_t, gbest);
+  else
+    stream_run<TIn, MODE_CANDS>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first, m_t, s_t,
+                                gbest);
+  cbar();
+  // ---- the record: the delegates (unsorted), the threshold, the sum of rows without top-k
+  float m = -INFINITY, sum = 0.f;
+  if (need_sum) {
+    const uint32_t mk = cta_max_u32(okey(m_t == -FLT_MAX ? -INFINITY : m_t), S);
+    m = from_okey(mk);
+    const float part = (m_t == -FLT_MAX) ? 0.f : s_t * ex2((m_t - m) * c2);
+    cta_excl_scan_f(part, &sum, S);
+  }
+  int n = 0;
+  if (!cands) {
+    const unsigned long long b = cta_min_u64(gbest, S);
+    if (b != ~0ull) {
+      if (tid == 0) ent[0] = b;
+      n = 1;
+    }
+  } else if (S.sc[SC_NC] > CAND_CAP) {
+    flags |= REC_OVERFLOW;  // ties of the threshold flooded the list: exact search
+  } else {
+    n = S.sc[SC_NC];
+    for (int i = tid; i < n; i += NT) ent[i] = S.cand[i];
+  }
+  if (tid == 0) {
+    hd->m = m;
+    hd->s = sum;
+    hd->ylo_key = S.ylo_key;
+    hd->n = n;
+    hd->flags = flags;
+  }
+}
+
+template <typename TIn>
+__global__ void __launch_bounds__(NT, 3) k_stream(const KParams P) {
+  extern __shared__ __align__(128) unsigned char smraw[];
+  Smem& S = *reinterpret_cast<Smem*>(smraw);
+  // k_finish may be scheduled as soon as SMs free up; it waits for this grid's records itself
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int s0 = seg_begin(P, blockIdx.x), s1 = seg_begin(P, blockIdx.x + 1);
+  int sg = s0;
+  while (sg < s1) {
+    const int row = sg / P.nseg;
+    const int seg_a = sg - row * P.nseg;
+    const int seg_b = min(s1 - row * P.nseg, P.nseg) - 1;
+    run<TIn>(P, S, row, seg_a, seg_b);
+    cbar();
+    sg = row * P.nseg + seg_b + 1;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// k_finish: one CTA per row gathers its runs' records, selects, cuts and draws (or writes this
+// rank's shard record), falling back to the exact search when the candidates cannot decide the
+// row
+// ---------------------------------------------------------------------------------------------
+template <typename TIn>
+__global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
+  using E = Elem<TIn>;
+  extern __shared__ __align__(128) unsigned char smraw[];
+  Smem& S = *reinterpret_cast<Smem*>(smraw);
+  const int tid = threadIdx.x;
+  const int row = blockIdx.x;
+  const RowCfg c = load_row(P, row);
+  const int r0 = seg_owner(P, row * P.nseg);
+  const int nruns = seg_owner(P, row * P.nseg + P.nseg - 1) - r0 + 1;
+  const unsigned char* base = P.recs + (size_t)row * P.nseg * REC_STRIDE;
+  const TIn* rowp = (const TIn*)P.logits + (int64_t)row * P.ld;
+  RunRec* rh = reinterpret_cast<RunRec*>(S.mh);  // the run headers (32 bytes each)
+  static_assert(sizeof(RunRec) == sizeof(RecHdr), "run headers fit Smem::mh");
+  // the candidate list lives in the first half of scratch, the row's history in the second
+  unsigned long long* cand = S.scratch;
+  constexpr int FCAP = SCRATCH / 2;  // candidates; also history entries staged
+  if (tid < nruns) {
+    // the end of run tid: its CTA's last segment of this row
+    const int se = min(seg_begin(P, r0 + tid + 1) - row * P.nseg, P.nseg);
+    S.rhi[tid] = (int)(P.voff + min(P.V, (int64_t)se * P.seg_len));
+  }
+  if (tid == 0) S.sc[SC_NH] = 0;
+  if (c.pen && tid < 32) {  // the row's history entries inside this shard
+    const int64_t a = __ldg(P.hrow + row), b = __ldg(P.hrow + row + 1);
+    const int lane = tid;
+    const int64_t ia = warp_lower_bound(P.hids, a, b, P.voff, lane);
+    const int64_t ib = warp_lower_bound(P.hids, ia, b, P.voff + P.V, lane);
+    if (lane == 0) {
+      S.hpos = ia;
+      S.sc[SC_NH] = (int)(ib - ia);
+    }
+  }
+  cbar();
+  const bool greedy_plain = c.greedy && !c.pen;
+  const int K = c.greedy ? 1 : c.K;
+  // stage the history (ids, then counts) in the second half of scratch
+  const int nh = S.sc[SC_NH];
+  RunHist h;
+  h.n = nh;
+  {
+    // the second half of scratch: FCAP 8-byte words, room for FCAP ids and FCAP counts
+    h.shared = nh <= FCAP;
+    int* hid = reinterpret_cast<int*>(S.scratch + FCAP);
+    if (h.shared) {
+      for (int j = tid; j < nh; j += NT) {
+        hid[j] = __ldg(P.hids + S.hpos + j);
+        hid[nh + j] = __ldg(P.hcnt + S.hpos + j);
+      }
+      h.ids = hid;
+      h.cnt = hid + nh;
+    } else {
+      h.ids = P.hids + S.hpos;
+      h.cnt = P.hcnt + S.hpos;
+    }
+  }
+  // everything above reads inputs only; the run records come from k_stream
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (tid < nruns) rh[tid] = *reinterpret_cast<const RunRec*>(base + (size_t)tid * REC_STRIDE);
+  cbar();
+  if (tid == 0) {
+    uint32_t fl = 0;
+    float m = -INFINITY;
+    int tot = 0;
+    for (int r = 0; r < nruns; ++r) {
+      fl |= rh[r].flags;
+      m = fmaxf(m, rh[r].m);
+      S.moff[r] = tot;
+      tot += rh[r].n;
+    }
+    S.moff[nruns] = tot;
+    float sum = 0.f;
+    if (c.need_sum)
+      for (int r = 0; r < nruns; ++r)
+        if (rh[r].m > -INFINITY) sum += rh[r].s * ex2((rh[r].m - m) * c.c2);
+    S.sc[SC_X0] = (int)fl;
+    S.sf[SF_M] = m;
+    S.sf[SF_SK] = sum;
+    S.sc[SC_NC] = 0;
+    S.dkth = ~0ull;
+  }
+  cbar();
+  uint32_t flags = (uint32_t)S.sc[SC_X0];
+  const float m_y = S.sf[SF_M];
+  float s_run = S.sf[SF_SK];
+  const int ntot = S.moff[nruns];
+  const bool local = P.mode == 1;
+  unsigned char* shard = local ? P.shard_out + (size_t)row * P.shard_stride : nullptr;
+  if (flags & REC_BAD) {
+    if (tid == 0) {
+      if (local) {
+        write_flag_hdr(reinterpret_cast<RecHdr*>(shard), REC_BAD, m_y, s_run);
+      } else {
         write_state(P, row, 3, -1, 0.f, 0.f, 0u, 0);
         status_or(P, VINFER_ST_BAD_PARAM);
       }
-      return;
     }
-    bool done = false;
-    if (!(flags & (REC_OVERFLOW | REC_EXACT))) {
-      MergeIn m;
-      m.m_y = m_y;
-      m.s = s_run;
-      m.d_key = tkey;
-      m.flags = flags;
-      m.n = nret;
-      done = finalize_sorted(P, c, row, m, sorted, S);
+    return;
+  }
+  bool exact = (flags & (REC_EXACT | REC_OVERFLOW)) != 0 || ntot > CAND_BUF;
+  int nret = 0;
+  uint32_t dkey = 0, rflags = 0;
+  RowCfg cq{};  // what vf() needs
+  cq.T = c.T;
+  cq.greedy = c.greedy;
+  // the run of global id `id` (of this shard)
+  auto run_of = [&](int id) {
+    int r = 0;
+    while (r < nruns - 1 && id >= S.rhi[r]) ++r;
+    return r;
+  };
+  if (!exact) {
+    // ---- the runs' delegates (or greedy entries)
+    for (int idx = tid; idx < ntot; idx += NT) {
+      int r = 0;
+      while (S.moff[r + 1] <= idx) ++r;
+      const unsigned long long* re = reinterpret_cast<const unsigned long long*>(
+          base + (size_t)r * REC_STRIDE + sizeof(RunRec));
+      unsigned long long x = __ldcg(re + (idx - S.moff[r]));
+      if (!greedy_plain && c.pen) {  // delegates holding a history id do not bound the K-th
+        const uint32_t lo32 = (uint32_t)x;
+        if (hist_any(h, (int)(lo32 & DL_ID), (lo32 & DL_ONE) ? 1 : E::A)) x |= DL_PEN;
+      }
+      S.cand[idx] = x;
     }
     cbar();
-    if (!done) exact_row<TIn>(P, c, row, S, scratch);
-    return;
-  }
-  // write the record: this run's slot of the row, or this rank's shard record (single run)
-  const bool shard = nruns == 1;  // local mode with the whole row here
-  unsigned char* rec = shard ? P.shard_out + (size_t)row * P.shard_stride
-                             : P.recs + ((size_t)row * P.nseg + run_idx) * REC_STRIDE;
-  const int cap = shard ? P.shard_cap : CAND_CAP;
-  if (nret > cap && !(flags & (REC_BAD | REC_EXACT))) flags = REC_OVERFLOW;
-  RecHdr* h = (RecHdr*)rec;
-  unsigned long long* ent = (unsigned long long*)(rec + sizeof(RecHdr));
-  const bool listed = !(flags & (REC_BAD | REC_EXACT | REC_OVERFLOW));
-  if (listed)
-    for (int j = tid; j < nret; j += NT) ent[j] = sorted[j];
-  if (tid == 0) {
-    h->m_y = m_y;
-    h->s = s_run;
-    h->n = listed ? nret : 0;
-    h->t_key = listed ? tkey : 0u;
-    h->flags = flags;
-  }
-  if (shard) return;
-  // the CTA that completes the row merges it
-  __threadfence();
-  cbar();
-  if (tid == 0) {
-    const int old = atom_add_acq_rel(&P.counters[row], 1);
-    const int last = old == nruns - 1;
-    if (last) P.counters[row] = 0;  // ready for the next call
-    S.sc[SC_LAST] = last;
-  }
-  cbar();
-  if (!S.sc[SC_LAST]) return;
-  finish_row<TIn>(P, S, scratch, row, P.recs + (size_t)row * P.nseg * REC_STRIDE, REC_STRIDE,
-                  nruns, P.mode == 1, nullptr);
-}
-
-template <typename TIn>
-__device__ void consumer(const KParams& P, Smem& S) {
-  const int tid = threadIdx.x;
-  const int s0 = seg_begin(P, blockIdx.x), s1 = seg_begin(P, blockIdx.x + 1);
-  RowCfg c{};
-  RunState R{};
-  int first_seg = 0;
-  for (int i = 0; s0 + i < s1; ++i) {
-    const int sg = s0 + i, row = sg / P.nseg, seg = sg - row * P.nseg;
-    const int s = i % NSTAGE, use = i / NSTAGE;
-    Stage& st = S.st[s];
-    const bool ok = mbar_wait_bounded(&S.full[s], use & 1);
-    if (cbar_or(!ok)) {
-      mbar_wait_bounded(&S.full[s], use & 1);  // a copy may still be in flight
-      if (tid == 0) status_or(P, VINFER_ST_TIMEOUT);
-      return;
-    }
-    if (i == 0 || seg == 0) {  // a new run
-      c = cfg_from(P, st.prm);
-      R.m_t = -FLT_MAX;
-      R.s_t = 0.f;
-      R.gbest = ~0ull;
-      first_seg = seg;
-      if (tid == 0) {
-        S.sc[SC_NC] = 0;
-        S.sc[SC_RFL] = 0;
-        S.sf[SF_YLO] = __int_as_float(0x7fc00000);  // NaN: no threshold yet
+    if (greedy_plain) {
+      // one entry per run: the smallest composite key is the first index of the maximum
+      unsigned long long b = ~0ull;
+      for (int i = 0; i < ntot; ++i) b = S.cand[i] < b ? S.cand[i] : b;
+      if (tid == 0) cand[0] = b;
+      nret = b != ~0ull;
+      rflags = (nret && P.V > 1) ? REC_UNRETAINED : 0u;
+      dkey = nret ? comp_key(b) : 0u;
+      cbar();
+    } else {
+      // ---- the row's K-th largest unflagged delegate: K distinct vectors reach it
+      for (int idx = tid; idx < ntot; idx += NT) {
+        const unsigned long long x = S.cand[idx];
+        if ((uint32_t)x & DL_PEN) continue;
+        int rank = 0;
+#pragma unroll 8
+        for (int q = 0; q < ntot; ++q) {
+          const unsigned long long y = S.cand[q];
+          rank += !((uint32_t)y & DL_PEN) && y < x;
+        }
+        if (rank == K - 1) S.dkth = x;
       }
       cbar();
-    }
-    if (!(c.bad || c.exact) && !(S.sc[SC_RFL] & RUN_OVER)) {
-      const Geo g = geometry<TIn>(P, row, seg);
-      run_segment<TIn>(P, c, g, st, S, R);  // ends with a consumer barrier
-    }
-    if (sg + 1 == s1 || seg == P.nseg - 1) {
-      run_end<TIn>(P, c, row, first_seg, seg, S, R, st.data);
+      if (tid < 32) {
+        float y = -INFINITY;
+        if (S.dkth != ~0ull) y = ylo_for(vf(dele_max(S.dkth), cq), cq);
+        // each run's final threshold: its own, or the row's bound when that is higher
+        for (int r = tid; r < nruns; r += 32) {
+          const float yr = fmaxf(from_okey(rh[r].ylo_key), y);
+          rh[r].ylo_key = okey(yr);
+        }
+      }
       cbar();
+      // ---- expansion: delegates at or above their run's final threshold are read again and
+      //      every non-penalised element at or above it becomes a candidate
+      auto emit = [&](float y, int id, float ylo) {
+        if (!(y >= ylo)) return;
+        if (c.pen && hist_count(h, id) > 0) return;
+        const int pos = atomicAdd(&S.sc[SC_NC], 1);
+        if (pos < FCAP) cand[pos] = comp(okey(vf(y, cq)), id);
+      };
+      for (int idx = tid; idx < ntot; idx += NT) {
+        const unsigned long long x = S.cand[idx];
+        const int id0 = (int)((uint32_t)x & DL_ID);
+        const float ylo = from_okey(rh[run_of(id0)].ylo_key);
+        if (!(dele_max(x) >= ylo)) continue;
+        const int64_t li = (int64_t)id0 - P.voff;
+        if ((uint32_t)x & DL_ONE) {
+          emit(E::ld(rowp, li), id0, ylo);
+        } else {
+          const uint4 q = __ldg(reinterpret_cast<const uint4*>(rowp + li));
+#pragma unroll
+          for (int e = 0; e < E::A; ++e) emit(E::at(q, e), id0 + e, ylo);
+        }
+      }
+      // ---- the penalised tokens with their exact values; their terms in the sum replaced
+      if (c.pen) {
+        float draw = 0.f, dtrue = 0.f;
+        constexpr int PB = 8;  // entries per thread whose logits are fetched together
+        for (int j0 = 0; j0 < nh; j0 += PB * NT) {
+          int id[PB], cn[PB];
+          float raw[PB];
+#pragma unroll
+          for (int k = 0; k < PB; ++k) {
+            const int j = j0 + k * NT + tid;
+            id[k] = j < nh ? (h.shared ? h.ids[j] : __ldg(h.ids + j)) : 0;
+            cn[k] = j < nh ? (h.shared ? h.cnt[j] : __ldg(h.cnt + j)) : 0;
+          }
+#pragma unroll
+          for (int k = 0; k < PB; ++k)
+            raw[k] = cn[k] > 0 ? E::ld(rowp, (int64_t)id[k] - P.voff) : 0.f;
+#pragma unroll
+          for (int k = 0; k < PB; ++k) {
+            if (cn[k] <= 0) continue;
+            const float yt = penalize(raw[k], cn[k], c);
+            if (yt >= from_okey(rh[run_of(id[k])].ylo_key)) {
+              const int pos = atomicAdd(&S.sc[SC_NC], 1);
+              if (pos < FCAP) cand[pos] = comp(okey(vf(yt, c)), id[k]);
+            }
+            if (c.need_sum) {
+              draw += ex2((raw[k] - m_y) * c.c2);
+              dtrue += ex2((yt - m_y) * c.c2);
+            }
+          }
+        }
+        if (c.need_sum) {
+          float dr, dt;
+          cta_excl_scan_f(draw, &dr, S);
+          cta_excl_scan_f(dtrue, &dt, S);
+          if (dr > 0.5f * s_run) exact = true;  // cancellation: the exact search decides
+          s_run = s_run - dr + dt;
+        }
+      }
+      cbar();
+      const int nc = S.sc[SC_NC];
+      if (nc > FCAP) {
+        exact = true;
+      } else {
+        uint32_t tkey;
+        nret = select_inplace(cand, nc, K, &tkey, S);
+        // every element at or above each run's threshold is a candidate; the top-K cut is
+        // known only when the K-th candidate reaches all of them
+        uint32_t maxkey = 0;
+        bool all_in = true;
+        for (int r = 0; r < nruns; ++r) {
+          const float y = from_okey(rh[r].ylo_key);
+          if (y > -INFINITY) {
+            all_in = false;
+            maxkey = max(maxkey, okey(vf(y, cq)));
+          }
+        }
+        const bool cut_ok = all_in || (nc >= K && tkey >= maxkey);
+        if ((c.topk || c.greedy) && !cut_ok) exact = true;
+        const bool more = !(all_in && nret == nc);
+        dkey = max(nc >= K ? tkey : 0u, maxkey);
+        rflags = more ? REC_UNRETAINED : 0u;
+      }
     }
-    if (tid == 0) mbar_arrive(&S.empty[s]);
   }
-}
-
-// ---------------------------------------------------------------------------------------------
-// kernels
-// ---------------------------------------------------------------------------------------------
-template <typename TIn>
-__global__ void __launch_bounds__(NTHR, 2) k_sample(const KParams P) {
-  extern __shared__ __align__(128) unsigned char smraw[];
-  Smem& S = *reinterpret_cast<Smem*>(smraw);
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < NSTAGE; ++s) {
-      mbar_init(&S.full[s], 1);
-      mbar_init(&S.empty[s], 1);
+  if (local) {  // this rank's shard record: the sorted entries and the completeness key
+    RecHdr* oh = reinterpret_cast<RecHdr*>(shard);
+    unsigned long long* oe = reinterpret_cast<unsigned long long*>(shard + sizeof(RecHdr));
+    if (exact || nret > P.shard_cap) {
+      if (tid == 0) write_flag_hdr(oh, REC_OVERFLOW, m_y, s_run);
+      return;
     }
-    mbar_fence_init();
-  }
-  __syncthreads();
-  if (threadIdx.x >= NT) {
-    producer<TIn>(P, S);
+    for (int j = tid; j < nret; j += NT) oe[j] = cand[j];
+    if (tid == 0) {
+      oh->m_y = m_y;
+      oh->s = s_run;
+      oh->n = nret;
+      oh->t_key = rflags ? dkey : 0u;
+      oh->flags = rflags;
+    }
     return;
   }
-  consumer<TIn>(P, S);
+  bool done = false;
+  if (!exact) {
+    MergeIn mi;
+    mi.m_y = m_y;
+    mi.s = s_run;
+    mi.d_key = dkey;
+    mi.flags = rflags;
+    mi.n = nret;
+    if (nret >= 1 && nret <= 64 && !c.greedy) {  // one warp, no CTA barriers
+      if (tid < 32) {
+        const bool d = finalize_warp(P, c, row, mi, cand);
+        if (tid == 0) S.sc[SC_X1] = d;
+      }
+      cbar();
+      done = S.sc[SC_X1] != 0;
+    } else {
+      done = finalize_sorted(P, c, row, mi, cand, S);
+    }
+  }
+  cbar();
+  if (!done) exact_row<TIn>(P, c, row, S, reinterpret_cast<unsigned char*>(S.scratch));
 }
 
-// merge of gathered shard records: one CTA of consumer threads per row
+// ---------------------------------------------------------------------------------------------
+// kernels: sharded merge and probabilities
+// ---------------------------------------------------------------------------------------------
+// merge of gathered shard records: one CTA per row
 template <typename TIn>
 __global__ void __launch_bounds__(NT, 1) k_merge(const KParams P, const unsigned char* recs,
                                               int world, int* unresolved) {
   extern __shared__ __align__(128) unsigned char smraw[];
   Smem& S = *reinterpret_cast<Smem*>(smraw);
   const int row = blockIdx.x;
-  finish_row<TIn>(P, S, S.st[0].data, row, recs + (size_t)row * P.shard_stride,
+  finish_row<TIn>(P, S, (unsigned char*)S.scratch, row, recs + (size_t)row * P.shard_stride,
                   (size_t)P.B * P.shard_stride, world, false, unresolved);
 }
 
@@ -1772,28 +2059,23 @@ struct Shape {
   int nseg, seg_len, grid;
 };
 
-// Segments per row and CTAs for a batch. With fewer rows than CTAs, each row is split into
-// c = ctas / B runs of whole segments (nseg a multiple of c), so every CTA streams one run and
-// only split rows need a merge; with more rows than CTAs, the CTAs share the row-major list of
-// segments in equal contiguous ranges.
+// Segments per row and CTAs for a batch. A row is cut into at least enough segments of at most
+// SEG_BYTES, and into more (down to 2048 tokens) when the batch has fewer rows than the device
+// has resident CTAs. The grid takes min(segments, ctas) CTAs, which share the row-major list of
+// segments in equal contiguous ranges: every CTA streams the same number of bytes.
 Shape plan(int64_t B, int64_t V, int dtype, int ctas) {
   const int es = dtype == VINFER_DTYPE_BF16 ? 2 : 4;
   const int A = 16 / es;
   const int64_t min_seg = (V * es + SEG_BYTES - 1) / SEG_BYTES;
-  int64_t c = 1;
-  if (B < ctas) c = std::min<int64_t>(ctas / B, MAX_NSEG);
-  c = std::max<int64_t>(1, std::min<int64_t>(c, V / 2048));  // segments of >= 2048 tokens
-  int64_t nseg = std::max<int64_t>(min_seg, c);
-  nseg = (nseg + c - 1) / c * c;
-  nseg = std::min<int64_t>(nseg, MAX_NSEG);
+  int64_t want = std::min<int64_t>(std::min<int64_t>(MAX_NSEG, ctas / B), V / 2048);
+  int64_t nseg = std::max<int64_t>(min_seg, want);
   int64_t len = (V + nseg - 1) / nseg;
   len = (len + A - 1) / A * A;
   nseg = (V + len - 1) / len;
   Shape s;
   s.nseg = (int)nseg;
   s.seg_len = (int)len;
-  const int64_t total = B * nseg;
-  s.grid = (int)std::min<int64_t>(total, B < ctas ? B * c : ctas);
+  s.grid = (int)std::min<int64_t>(B * nseg, ctas);
   return s;
 }
 
@@ -1803,11 +2085,10 @@ size_t align_up(size_t x) { return (x + ALIGN - 1) / ALIGN * ALIGN; }
 struct WsLayout {
   size_t counters, rows, recs, total;
 };
-// Records: one slot per (row, run). Rows are split into at most nseg runs; nseg is at most
-// MAX_NSEG when rows may be split for parallelism (B below the resident-CTA bound), otherwise
-// the count the segment size alone needs.
+// Records: one slot per (row, run); a row has at most nseg runs. The plan's nseg never
+// decreases with the CTA count, so the plan at the CTA cap bounds every device.
 WsLayout ws_layout(int64_t B, int64_t V, int dtype) {
-  const int64_t nseg = B < CTA_CAP ? MAX_NSEG : plan(B, V, dtype, CTA_CAP).nseg;
+  const int64_t nseg = plan(B, V, dtype, CTA_CAP).nseg;
   WsLayout L;
   L.counters = 0;
   L.rows = align_up((size_t)B * sizeof(int));
@@ -1871,7 +2152,7 @@ struct KernInfo {
   int ctas;
 };
 int kernel_info(const void* kern, int slot, int threads, int* ctas) {
-  static KernInfo info[64][4] = {};
+  static KernInfo info[64][6] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VINFER_E_CUDA;
   KernInfo& k = info[dev][slot];
@@ -1894,21 +2175,39 @@ int kernel_info(const void* kern, int slot, int threads, int* ctas) {
 
 // resident CTAs of k_sample on the current device (at most CTA_CAP)
 int sample_ctas(int dtype, int* ctas) {
-  const void* kern = dtype == VINFER_DTYPE_BF16 ? (const void*)k_sample<__nv_bfloat16>
-                                                : (const void*)k_sample<float>;
-  if (kernel_info(kern, dtype == VINFER_DTYPE_BF16 ? 0 : 1, NTHR, ctas) != VINFER_OK)
+  const void* kern = dtype == VINFER_DTYPE_BF16 ? (const void*)k_stream<__nv_bfloat16>
+                                                : (const void*)k_stream<float>;
+  if (kernel_info(kern, dtype == VINFER_DTYPE_BF16 ? 0 : 1, NT, ctas) != VINFER_OK)
     return VINFER_E_CUDA;
   *ctas = std::min(*ctas, CTA_CAP);
   return VINFER_OK;
 }
 
+// the streaming pass, then one finishing CTA per row (mode 0: answer, mode 1: shard record)
 int launch_sample(const KParams& P, int dtype, cudaStream_t st) {
-  const dim3 grid(P.grid);
-  if (dtype == VINFER_DTYPE_BF16) k_sample<__nv_bfloat16><<<grid, NTHR, sizeof(Smem), st>>>(P);
-  else k_sample<float><<<grid, NTHR, sizeof(Smem), st>>>(P);
-  return cudaGetLastError() == cudaSuccess ? VINFER_OK : VINFER_E_CUDA;
+  const bool bf = dtype == VINFER_DTYPE_BF16;
+  const void* fin = bf ? (const void*)k_finish<__nv_bfloat16> : (const void*)k_finish<float>;
+  int unused = 0;
+  if (kernel_info(fin, bf ? 4 : 5, NT, &unused) != VINFER_OK) return VINFER_E_CUDA;
+  if (bf) k_stream<__nv_bfloat16><<<P.grid, NT, sizeof(Smem), st>>>(P);
+  else k_stream<float><<<P.grid, NT, sizeof(Smem), st>>>(P);
+  if (cudaGetLastError() != cudaSuccess) return VINFER_E_CUDA;
+  // programmatic dependent launch: k_finish starts on SMs as k_stream frees them and does its
+  // input-only set-up before waiting for k_stream's records
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)P.B);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = sizeof(Smem);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = bf ? cudaLaunchKernelEx(&cfg, k_finish<__nv_bfloat16>, P)
+                           : cudaLaunchKernelEx(&cfg, k_finish<float>, P);
+  return e == cudaSuccess ? VINFER_OK : VINFER_E_CUDA;
 }
-
 int launch_probs(const KParams& P, int dtype, cudaStream_t st) {
   if (!P.out_probs) return VINFER_OK;
   const int bx = (int)std::min<int64_t>(64, (P.V + 256 * 8 - 1) / (256 * 8));
