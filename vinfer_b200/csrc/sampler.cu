@@ -152,9 +152,8 @@ struct __align__(16) Smem {
 };
 
 // scalar slots in Smem::sc / Smem::sf
-enum { SC_NC = 0, SC_NRET, SC_TKEY, SC_LAST, SC_B, SC_J, SC_X0, SC_X1, SC_NQ, SC_RFL, SC_NH };
-// run flags in Smem::sc[SC_RFL]
-constexpr int RUN_OVER = 1;  // the candidate buffer overflowed
+enum { SC_NC = 0, SC_NRET, SC_TKEY, SC_LAST, SC_B, SC_J, SC_X0, SC_X1, SC_NQ, SC_RFL, SC_NH,
+       SC_FB };
 enum { SF_TH = 0, SF_SK = 2, SF_M };
 
 // ---------------------------------------------------------------------------------------------
@@ -185,15 +184,10 @@ __device__ __forceinline__ void status_or(const KParams& P, uint32_t bits) {
 }
 // CTA barrier (named barrier 1 over all threads)
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
-__device__ __forceinline__ bool cbar_or(bool p) {
-  uint32_t r;
-  asm volatile(
-      "{\n .reg .pred a, b;\n setp.ne.u32 a, %1, 0;\n bar.red.or.pred b, 1, %2, a;\n"
-      " selp.u32 %0, 1, 0, b;\n}\n"
-      : "=r"(r)
-      : "r"((uint32_t)p), "n"(NT)
-      : "memory");
-  return r != 0;
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
   int old;
@@ -1266,26 +1260,13 @@ __device__ __forceinline__ RunHist hist_view(const KParams& P, Smem& S) {
   }
   return h;
 }
-__device__ __forceinline__ int hist_count(const RunHist& h, int id) {
-  int a = 0, b = h.n;
-  while (a < b) {
-    const int mid = (a + b) >> 1;
-    const int v = h.shared ? h.ids[mid] : __ldg(h.ids + mid);
-    if (v < id) a = mid + 1; else b = mid;
-  }
-  if (a >= h.n) return 0;
-  const int v = h.shared ? h.ids[a] : __ldg(h.ids + a);
-  if (v != id) return 0;
-  return h.shared ? h.cnt[a] : __ldg(h.cnt + a);
-}
 
 // ---- delegates --------------------------------------------------------------------------------
 // While streaming, a vector (or an edge element) whose maximum reaches the threshold is only
 // noted: its maximum raw logit and the id of its first element. At the end of the run the K-th
 // largest delegate bounds the run's K-th largest value closely, and only the vectors at or above
-// that bound are read again and expanded. Entry: (~okey(max) << 32) | flags | first id, so
-// ascending entries are descending maxima.
-constexpr uint32_t DL_PEN = 0x80000000u;  // a history id falls inside: the max may be penalised
+// that bound are read again and expanded. Entry: (~okey(max) << 32) | DL_ONE flag | first
+// id, so ascending entries are descending maxima.
 constexpr uint32_t DL_ONE = 0x40000000u;  // an edge element, not a 16-byte vector
 constexpr uint32_t DL_ID = 0x3FFFFFFFu;
 static_assert(2 * (int64_t)VINFER_MAX_VOCAB <= (int64_t)DL_ID, "global ids fit a delegate");
@@ -1409,71 +1390,114 @@ __device__ __forceinline__ void load_segment(const KParams& P, const TIn* rowp, 
   }
 }
 
-// The run's first threshold, from its first segment (CTA-wide, once per run): each warp sorts
-// its lanes' largest vector maxima (a bitonic sort of (value, vector) pairs) and publishes its
-// kk = min(K, 32) best, leaving out vectors that hold a history id (their maximum may be a
-// penalised token); the K-th largest of the 8 * kk published values is reached by K distinct
-// vectors, so it bounds the run's K-th largest processed value from below.
-template <typename TIn>
-__device__ __forceinline__ void cta_first_bound(const KParams& P, const SegLoad<TIn>& L,
-                                                const float* vm, int K, float T, bool greedy,
-                                                bool pen, Smem& S) {
-  constexpr int A = Elem<TIn>::A;
-  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  float lv = -INFINITY;
-  int lid = -1;
+// ---- warp-level sorting helpers (ascending 64-bit keys across the 32 lanes) -----------------
+__device__ __forceinline__ unsigned long long warp_sort32(unsigned long long x) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int u = 0; u < U; ++u) {
-    if (vm[u] > lv) {
-      lv = vm[u];
-      lid = (int)(L.gid0 + (int64_t)(tid + NT * u) * A);
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const unsigned long long o = __shfl_xor_sync(FULLMASK, x, j);
+      const bool lower = (lane & j) == 0, up = (lane & k) == 0;
+      x = (lower == up) ? (o < x ? o : x) : (o > x ? o : x);
     }
   }
+  return x;
+}
+// the 32 smallest of two ascending lane-sorted lists, ascending
+__device__ __forceinline__ unsigned long long warp_merge32(unsigned long long a,
+                                                           unsigned long long b) {
+  const int lane = threadIdx.x & 31;
+  const unsigned long long r = __shfl_sync(FULLMASK, b, 31 - lane);
+  unsigned long long x = r < a ? r : a;  // a bitonic sequence holding the 32 smallest
 #pragma unroll
-  for (int k = 2; k <= 32; k <<= 1) {  // descending bitonic sort of the pairs
+  for (int j = 16; j > 0; j >>= 1) {
+    const unsigned long long o = __shfl_xor_sync(FULLMASK, x, j);
+    x = ((lane & j) == 0) ? (o < x ? o : x) : (o > x ? o : x);
+  }
+  return x;
+}
+
+// A first threshold for the run from this warp's first segment, with no CTA barrier: each lane
+// takes the j-th largest of its vector maxima (j = ceil(K / 32)), and if q = ceil(K / j) lanes
+// reach t then K distinct vectors do. t is the q-th largest lane value (a warp bitonic sort).
+// With j = 1 a lane whose best vector holds a history id contributes nothing, so penalised
+// tokens cannot lift the bound; with j > 1 they are not checked, and should penalties push
+// the bound above the row's K-th largest processed value, the finishing kernel detects it and
+// takes the exact search, so it only ever costs time. Published with atomicMax.
+template <typename TIn>
+__device__ __forceinline__ void warp_first_bound(const KParams& P, const SegLoad<TIn>& L,
+                                                 const float* vm, int K, float T, bool greedy,
+                                                 bool pen, Smem& S) {
+  constexpr int A = Elem<TIn>::A;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int j = (K + 31) / 32;
+  float v[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) v[u] = vm[u];
+  float lv = -INFINITY;
+  int um = -1;
+  for (int r = 0; r < j; ++r) {  // j-th largest of the lane's vector maxima
+    float m = -INFINITY;
+    int mu = -1;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (v[u] > m) {
+        m = v[u];
+        mu = u;
+      }
+    lv = m;
+    um = mu;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (u == mu) v[u] = -INFINITY;
+  }
+  if (j == 1 && pen && um >= 0 &&
+      hist_any(hist_view(P, S), (int)(L.gid0 + (int64_t)(tid + NT * um) * A), A))
+    lv = -INFINITY;
+  float x = lv;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {  // descending bitonic sort of the 32 lane values
 #pragma unroll
     for (int jj = k >> 1; jj > 0; jj >>= 1) {
-      const float ov = __shfl_xor_sync(FULLMASK, lv, jj);
-      const int oid = __shfl_xor_sync(FULLMASK, lid, jj);
-      const bool take_max = ((lane & jj) == 0) == ((lane & k) == 0);
-      if (take_max ? (ov > lv) : (ov < lv)) {
-        lv = ov;
-        lid = oid;
-      }
+      const float o = __shfl_xor_sync(FULLMASK, x, jj);
+      const bool lower = (lane & jj) == 0, up = (lane & k) == 0;
+      x = (lower == up) ? fmaxf(x, o) : fminf(x, o);
     }
   }
-  const int kk = min(K, 32);
-  if (lane < kk) {
-    float v = lv;
-    if (pen && lid >= 0 && hist_any(hist_view(P, S), lid, A)) v = -INFINITY;
-    S.ext[w * 32 + lane] = v;
+  const int q = (K + j - 1) / j;
+  const float t = __shfl_sync(FULLMASK, x, q - 1);
+  RowCfg c{};
+  c.T = T;
+  c.greedy = greedy;
+  if (t > -INFINITY) {
+    const float y = ylo_for(vf(t, c), c);
+    if (lane == 0) atomicMax(&S.ylo_key, okey(y));
   }
-  if (tid == 0) S.sf[SF_TH] = -INFINITY;  // fewer than K usable values: no bound
-  cbar();
-  if (lane < kk) {
-    const float x = S.ext[tid];
-    int rank = 0;
-    for (int o = 0; o < NCW; ++o) {
-#pragma unroll 8
-      for (int r = 0; r < kk; ++r) {
-        const float z = S.ext[o * 32 + r];
-        rank += (z > x) || (z == x && o * 32 + r < tid);
-      }
-    }
-    if (rank == K - 1 && x > -INFINITY) S.sf[SF_TH] = x;
-  }
-  cbar();
-  if (w == 0) {
-    const float th = S.sf[SF_TH];
-    if (th > -INFINITY) {
-      RowCfg c{};
-      c.T = T;
-      c.greedy = greedy;
-      const float y = ylo_for(vf(th, c), c);
+  // publish the sorted lane values; the last warp to do so derives the CTA-wide bound (the
+  // q-th largest of all 256 lane values) without making any warp wait
+  const int w = tid >> 5;
+  S.ext[w * 32 + lane] = x;
+  __threadfence_block();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = atomicAdd(&S.sc[SC_FB], 1) == NCW - 1;
+  if (__shfl_sync(FULLMASK, last, 0)) {
+    __threadfence_block();
+    const volatile float* ext = S.ext;
+    auto key = [&](int o) {  // ascending keys = descending values, unique by position
+      return ((unsigned long long)(~okey(ext[o * 32 + lane])) << 32) | (uint32_t)(o * 32 + lane);
+    };
+    unsigned long long m = key(0);
+    for (int o = 1; o < NCW; ++o) m = warp_merge32(m, key(o));
+    const unsigned long long kq = __shfl_sync(FULLMASK, m, q - 1);
+    const float tc = from_okey(~(uint32_t)(kq >> 32));
+    if (tc > -INFINITY) {
+      const float y = ylo_for(vf(tc, c), c);
       if (lane == 0) atomicMax(&S.ylo_key, okey(y));
     }
   }
-  cbar();
+  __syncwarp();
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -1550,7 +1574,7 @@ __device__ __forceinline__ void stream_run(const KParams& P, Smem& S, int row, i
       }
       return;
     }
-    if (seg == seg_a) cta_first_bound<TIn>(P, L, vm, K, T, greedy, pen, S);
+    if (seg == seg_a) warp_first_bound<TIn>(P, L, vm, K, T, greedy, pen, S);
     // the CTA's threshold as it stands: warps raise it as they go
     const float ylo = from_okey(*reinterpret_cast<volatile uint32_t*>(&S.ylo_key));
     int trig = -1;  // a block of the list this thread completed
@@ -1584,7 +1608,7 @@ __device__ __forceinline__ void stream_run(const KParams& P, Smem& S, int row, i
 // One run: segments seg_a..seg_b of `row`, streamed by the whole CTA, leaving its record.
 template <typename TIn>
 __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_a, int seg_b) {
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x;
   // the loop keeps only these scalars of the row's configuration
   bool greedy, pen, need_sum, active;
   float T, c2;
@@ -1612,19 +1636,13 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
   // ---- the history entries inside this run's ids, staged in shared memory
   if (tid == 0) S.sc[SC_NH] = 0;
   if (pen && active) {
-    if (tid < 32) {
-      const int64_t a = __ldg(P.hrow + row), b = __ldg(P.hrow + row + 1);
-      const int64_t ia = warp_lower_bound(P.hids, a, b, P.voff + (int64_t)seg_a * P.seg_len, lane);
-      const int64_t ib = warp_lower_bound(
-          P.hids, ia, b, P.voff + min(P.V, (int64_t)(seg_b + 1) * P.seg_len), lane);
-      if (lane == 0) {
-        S.hpos = ia;
-        S.sc[SC_NH] = (int)(ib - ia);
-      }
+    // the row's whole history (lookups only ever ask for ids of this run)
+    const int64_t ia = __ldg(P.hrow + row);
+    const int nh = (int)(__ldg(P.hrow + row + 1) - ia);
+    if (tid == 0) {
+      S.hpos = ia;
+      S.sc[SC_NH] = nh;
     }
-    cbar();
-    const int64_t ia = S.hpos;
-    const int nh = S.sc[SC_NH];
     if (nh <= HIST_CAP) {
       int* hid = reinterpret_cast<int*>(S.scratch);
       for (int j = tid; j < nh; j += NT) {
@@ -1634,8 +1652,9 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
     }
   }
   if (tid == 0) {
-    S.sc[SC_RFL] = 0;
     S.sc[SC_NC] = 0;
+    S.sc[SC_FB] = 0;
+    S.sc[SC_NRET] = 0;
     S.ylo_key = okey(-INFINITY);
     S.dkth = ~0ull;
   }
@@ -1650,6 +1669,8 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
       hd->ylo_key = 0u;
       hd->n = 0;
       hd->flags = flags;
+      __threadfence();
+      atom_add_acq_rel(&P.counters[row], 1);
     }
     return;
   }
@@ -1678,11 +1699,25 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
       if (tid == 0) ent[0] = b;
       n = 1;
     }
-  } else if (S.sc[SC_NC] > CAND_CAP) {
+  } else if (S.sc[SC_NC] > CAND_BUF) {
     flags |= REC_OVERFLOW;  // ties of the threshold flooded the list: exact search
   } else {
-    n = S.sc[SC_NC];
-    for (int i = tid; i < n; i += NT) ent[i] = S.cand[i];
+    // only the delegates at or above the final threshold can hold a candidate
+    const float ylo = from_okey(S.ylo_key);
+    const int nd = S.sc[SC_NC];
+    for (int i = tid; i < nd; i += NT) {
+      const unsigned long long x = S.cand[i];
+      if (dele_max(x) >= ylo) {
+        const int pos = atomicAdd(&S.sc[SC_NRET], 1);
+        if (pos < CAND_CAP) ent[pos] = x;
+      }
+    }
+    cbar();
+    n = S.sc[SC_NRET];
+    if (n > CAND_CAP) {
+      flags |= REC_OVERFLOW;
+      n = 0;
+    }
   }
   if (tid == 0) {
     hd->m = m;
@@ -1691,6 +1726,10 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
     hd->n = n;
     hd->flags = flags;
   }
+  // the record is complete: count it for the row (k_finish may be waiting on exactly this)
+  __threadfence();
+  cbar();
+  if (tid == 0) atom_add_acq_rel(&P.counters[row], 1);
 }
 
 template <typename TIn>
@@ -1716,12 +1755,22 @@ __global__ void __launch_bounds__(NT, 3) k_stream(const KParams P) {
 // rank's shard record), falling back to the exact search when the candidates cannot decide the
 // row
 // ---------------------------------------------------------------------------------------------
+// is `id` a penalised token of the row (present in the staged history with a positive count)?
+__device__ __forceinline__ bool hist_pen(const int* ids, const float* tv, int n, int id) {
+  int a = 0, b = n;
+  while (a < b) {
+    const int mid = (a + b) >> 1;
+    if (ids[mid] < id) a = mid + 1; else b = mid;
+  }
+  return a < n && ids[a] == id && tv[a] == tv[a];  // NaN marks a count <= 0
+}
+
 template <typename TIn>
 __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
   using E = Elem<TIn>;
   extern __shared__ __align__(128) unsigned char smraw[];
   Smem& S = *reinterpret_cast<Smem*>(smraw);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int row = blockIdx.x;
   const RowCfg c = load_row(P, row);
   const int r0 = seg_owner(P, row * P.nseg);
@@ -1730,9 +1779,12 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
   const TIn* rowp = (const TIn*)P.logits + (int64_t)row * P.ld;
   RunRec* rh = reinterpret_cast<RunRec*>(S.mh);  // the run headers (32 bytes each)
   static_assert(sizeof(RunRec) == sizeof(RecHdr), "run headers fit Smem::mh");
-  // the candidate list lives in the first half of scratch, the row's history in the second
+  // the candidate list lives in the first half of scratch, the row's history in the second:
+  // ids, then the penalised value of each entry (NaN when its count is not positive)
   unsigned long long* cand = S.scratch;
   constexpr int FCAP = SCRATCH / 2;  // candidates; also history entries staged
+  int* hid = reinterpret_cast<int*>(S.scratch + FCAP);
+  float* htv = reinterpret_cast<float*>(hid + FCAP);
   if (tid < nruns) {
     // the end of run tid: its CTA's last segment of this row
     const int se = min(seg_begin(P, r0 + tid + 1) - row * P.nseg, P.nseg);
@@ -1741,7 +1793,6 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
   if (tid == 0) S.sc[SC_NH] = 0;
   if (c.pen && tid < 32) {  // the row's history entries inside this shard
     const int64_t a = __ldg(P.hrow + row), b = __ldg(P.hrow + row + 1);
-    const int lane = tid;
     const int64_t ia = warp_lower_bound(P.hids, a, b, P.voff, lane);
     const int64_t ib = warp_lower_bound(P.hids, ia, b, P.voff + P.V, lane);
     if (lane == 0) {
@@ -1752,29 +1803,57 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
   cbar();
   const bool greedy_plain = c.greedy && !c.pen;
   const int K = c.greedy ? 1 : c.K;
-  // stage the history (ids, then counts) in the second half of scratch
   const int nh = S.sc[SC_NH];
-  RunHist h;
-  h.n = nh;
-  {
-    // the second half of scratch: FCAP 8-byte words, room for FCAP ids and FCAP counts
-    h.shared = nh <= FCAP;
-    int* hid = reinterpret_cast<int*>(S.scratch + FCAP);
-    if (h.shared) {
-      for (int j = tid; j < nh; j += NT) {
-        hid[j] = __ldg(P.hids + S.hpos + j);
-        hid[nh + j] = __ldg(P.hcnt + S.hpos + j);
+  const bool hshared = nh <= FCAP;
+  // ---- the penalised values of the history entries: inputs only, so before the wait
+  if (c.pen && hshared) {
+    constexpr int PB = 8;  // entries per thread whose ids and logits are fetched together
+    for (int j0 = 0; j0 < nh; j0 += PB * NT) {
+      int id[PB], cn[PB];
+      float raw[PB];
+#pragma unroll
+      for (int k = 0; k < PB; ++k) {
+        const int j = j0 + k * NT + tid;
+        id[k] = j < nh ? __ldg(P.hids + S.hpos + j) : 0;
+        cn[k] = j < nh ? __ldg(P.hcnt + S.hpos + j) : 0;
       }
-      h.ids = hid;
-      h.cnt = hid + nh;
-    } else {
-      h.ids = P.hids + S.hpos;
-      h.cnt = P.hcnt + S.hpos;
+#pragma unroll
+      for (int k = 0; k < PB; ++k)
+        raw[k] = cn[k] > 0 ? E::ld(rowp, (int64_t)id[k] - P.voff) : 0.f;
+#pragma unroll
+      for (int k = 0; k < PB; ++k) {
+        const int j = j0 + k * NT + tid;
+        if (j < nh) {
+          hid[j] = id[k];
+          htv[j] = cn[k] > 0 ? penalize(raw[k], cn[k], c) : __int_as_float(0x7fc00000);
+        }
+      }
     }
   }
-  // everything above reads inputs only; the run records come from k_stream
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (tid < nruns) rh[tid] = *reinterpret_cast<const RunRec*>(base + (size_t)tid * REC_STRIDE);
+  // everything above reads inputs only; the run records come from k_stream. The row is ready
+  // once all its runs have counted their records; a bounded wait for that, and should it run
+  // out, the wait for the whole streaming grid (which always ends).
+  if (tid == 0) {
+    int ready = 0;
+    for (int it = 0; it < 20000 && !ready; ++it) {
+      ready = ld_acquire(P.counters + row) >= nruns;
+      if (!ready) __nanosleep(128);
+    }
+    S.sc[SC_LAST] = ready;
+  }
+  cbar();
+  if (!S.sc[SC_LAST]) asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (tid < nruns) {
+    const RunRec* src = reinterpret_cast<const RunRec*>(base + (size_t)tid * REC_STRIDE);
+    RunRec r;
+    r.m = __ldcg(&src->m);
+    r.s = __ldcg(&src->s);
+    r.ylo_key = __ldcg(&src->ylo_key);
+    r.n = __ldcg(&src->n);
+    r.flags = __ldcg(&src->flags);
+    rh[tid] = r;
+  }
+  if (tid == 0) P.counters[row] = 0;  // ready for the next call (stream-ordered after this one)
   cbar();
   if (tid == 0) {
     uint32_t fl = 0;
@@ -1815,7 +1894,9 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
     }
     return;
   }
-  bool exact = (flags & (REC_EXACT | REC_OVERFLOW)) != 0 || ntot > CAND_BUF;
+  // with more history entries than the staging area holds, the row takes the exact search
+  bool exact = (flags & (REC_EXACT | REC_OVERFLOW)) != 0 || ntot > CAND_BUF ||
+               (c.pen && !hshared);
   int nret = 0;
   uint32_t dkey = 0, rflags = 0;
   RowCfg cq{};  // what vf() needs
@@ -1827,19 +1908,16 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
     while (r < nruns - 1 && id >= S.rhi[r]) ++r;
     return r;
   };
+  bool sorted_done = false;  // the candidates are sorted and cut (short-list path)
   if (!exact) {
-    // ---- the runs' delegates (or greedy entries)
+    // ---- the runs' delegates (or greedy entries); each run kept only those at or above its
+    //      final threshold
     for (int idx = tid; idx < ntot; idx += NT) {
       int r = 0;
       while (S.moff[r + 1] <= idx) ++r;
       const unsigned long long* re = reinterpret_cast<const unsigned long long*>(
           base + (size_t)r * REC_STRIDE + sizeof(RunRec));
-      unsigned long long x = __ldcg(re + (idx - S.moff[r]));
-      if (!greedy_plain && c.pen) {  // delegates holding a history id do not bound the K-th
-        const uint32_t lo32 = (uint32_t)x;
-        if (hist_any(h, (int)(lo32 & DL_ID), (lo32 & DL_ONE) ? 1 : E::A)) x |= DL_PEN;
-      }
-      S.cand[idx] = x;
+      S.cand[idx] = __ldcg(re + (idx - S.moff[r]));
     }
     cbar();
     if (greedy_plain) {
@@ -1852,34 +1930,11 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
       dkey = nret ? comp_key(b) : 0u;
       cbar();
     } else {
-      // ---- the row's K-th largest unflagged delegate: K distinct vectors reach it
-      for (int idx = tid; idx < ntot; idx += NT) {
-        const unsigned long long x = S.cand[idx];
-        if ((uint32_t)x & DL_PEN) continue;
-        int rank = 0;
-#pragma unroll 8
-        for (int q = 0; q < ntot; ++q) {
-          const unsigned long long y = S.cand[q];
-          rank += !((uint32_t)y & DL_PEN) && y < x;
-        }
-        if (rank == K - 1) S.dkth = x;
-      }
-      cbar();
-      if (tid < 32) {
-        float y = -INFINITY;
-        if (S.dkth != ~0ull) y = ylo_for(vf(dele_max(S.dkth), cq), cq);
-        // each run's final threshold: its own, or the row's bound when that is higher
-        for (int r = tid; r < nruns; r += 32) {
-          const float yr = fmaxf(from_okey(rh[r].ylo_key), y);
-          rh[r].ylo_key = okey(yr);
-        }
-      }
-      cbar();
-      // ---- expansion: delegates at or above their run's final threshold are read again and
-      //      every non-penalised element at or above it becomes a candidate
+      // ---- expansion: the delegates are read again and every non-penalised element at or
+      //      above its run's threshold becomes a candidate
       auto emit = [&](float y, int id, float ylo) {
         if (!(y >= ylo)) return;
-        if (c.pen && hist_count(h, id) > 0) return;
+        if (c.pen && hist_pen(hid, htv, nh, id)) return;
         const int pos = atomicAdd(&S.sc[SC_NC], 1);
         if (pos < FCAP) cand[pos] = comp(okey(vf(y, cq)), id);
       };
@@ -1897,37 +1952,25 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
           for (int e = 0; e < E::A; ++e) emit(E::at(q, e), id0 + e, ylo);
         }
       }
-      // ---- the penalised tokens with their exact values; their terms in the sum replaced
+      // ---- the penalised tokens with their exact values (computed before the wait)
       if (c.pen) {
-        float draw = 0.f, dtrue = 0.f;
-        constexpr int PB = 8;  // entries per thread whose logits are fetched together
-        for (int j0 = 0; j0 < nh; j0 += PB * NT) {
-          int id[PB], cn[PB];
-          float raw[PB];
-#pragma unroll
-          for (int k = 0; k < PB; ++k) {
-            const int j = j0 + k * NT + tid;
-            id[k] = j < nh ? (h.shared ? h.ids[j] : __ldg(h.ids + j)) : 0;
-            cn[k] = j < nh ? (h.shared ? h.cnt[j] : __ldg(h.cnt + j)) : 0;
-          }
-#pragma unroll
-          for (int k = 0; k < PB; ++k)
-            raw[k] = cn[k] > 0 ? E::ld(rowp, (int64_t)id[k] - P.voff) : 0.f;
-#pragma unroll
-          for (int k = 0; k < PB; ++k) {
-            if (cn[k] <= 0) continue;
-            const float yt = penalize(raw[k], cn[k], c);
-            if (yt >= from_okey(rh[run_of(id[k])].ylo_key)) {
-              const int pos = atomicAdd(&S.sc[SC_NC], 1);
-              if (pos < FCAP) cand[pos] = comp(okey(vf(yt, c)), id[k]);
-            }
-            if (c.need_sum) {
-              draw += ex2((raw[k] - m_y) * c.c2);
-              dtrue += ex2((yt - m_y) * c.c2);
-            }
+        for (int j = tid; j < nh; j += NT) {
+          const float yt = htv[j];
+          if (!(yt == yt)) continue;
+          if (yt >= from_okey(rh[run_of(hid[j])].ylo_key)) {
+            const int pos = atomicAdd(&S.sc[SC_NC], 1);
+            if (pos < FCAP) cand[pos] = comp(okey(vf(yt, c)), hid[j]);
           }
         }
-        if (c.need_sum) {
+        if (c.need_sum) {  // their terms in the softmax sum replaced
+          float draw = 0.f, dtrue = 0.f;
+          for (int j = tid; j < nh; j += NT) {
+            const float yt = htv[j];
+            if (!(yt == yt)) continue;
+            const float raw = E::ld(rowp, (int64_t)hid[j] - P.voff);
+            draw += ex2((raw - m_y) * c.c2);
+            dtrue += ex2((yt - m_y) * c.c2);
+          }
           float dr, dt;
           cta_excl_scan_f(draw, &dr, S);
           cta_excl_scan_f(dtrue, &dt, S);
@@ -1937,22 +1980,47 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
       }
       cbar();
       const int nc = S.sc[SC_NC];
+      uint32_t maxkey = 0;
+      bool all_in = true;
+      for (int r = 0; r < nruns; ++r) {
+        const float y = from_okey(rh[r].ylo_key);
+        if (y > -INFINITY) {
+          all_in = false;
+          maxkey = max(maxkey, okey(vf(y, cq)));
+        }
+      }
       if (nc > FCAP) {
         exact = true;
+      } else if (nc <= 32) {
+        // short list: one warp sorts it and applies the cut (no CTA barrier)
+        if (w == 0) {
+          unsigned long long x = lane < nc ? cand[lane] : ~0ull;
+          x = warp_sort32(x);
+          cand[lane] = x;
+          const unsigned long long kx = __shfl_sync(FULLMASK, x, min(K, 32) - 1);
+          const uint32_t tkey = nc >= K ? comp_key(kx) : 0u;
+          const int nr = nc >= K ? __popc(__ballot_sync(FULLMASK, lane < nc &&
+                                                                  comp_key(x) >= tkey))
+                                 : nc;
+          if (lane == 0) {
+            S.sc[SC_NRET] = nr;
+            S.sc[SC_TKEY] = (int)tkey;
+          }
+        }
+        cbar();
+        nret = S.sc[SC_NRET];
+        const uint32_t tkey = (uint32_t)S.sc[SC_TKEY];
+        const bool cut_ok = all_in || (nc >= K && tkey >= maxkey);
+        if ((c.topk || c.greedy) && !cut_ok) exact = true;
+        const bool more = !(all_in && nret == nc);
+        dkey = max(nc >= K ? tkey : 0u, maxkey);
+        rflags = more ? REC_UNRETAINED : 0u;
+        sorted_done = true;
       } else {
         uint32_t tkey;
         nret = select_inplace(cand, nc, K, &tkey, S);
         // every element at or above each run's threshold is a candidate; the top-K cut is
         // known only when the K-th candidate reaches all of them
-        uint32_t maxkey = 0;
-        bool all_in = true;
-        for (int r = 0; r < nruns; ++r) {
-          const float y = from_okey(rh[r].ylo_key);
-          if (y > -INFINITY) {
-            all_in = false;
-            maxkey = max(maxkey, okey(vf(y, cq)));
-          }
-        }
         const bool cut_ok = all_in || (nc >= K && tkey >= maxkey);
         if ((c.topk || c.greedy) && !cut_ok) exact = true;
         const bool more = !(all_in && nret == nc);
@@ -1961,6 +2029,7 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
       }
     }
   }
+  (void)sorted_done;
   if (local) {  // this rank's shard record: the sorted entries and the completeness key
     RecHdr* oh = reinterpret_cast<RecHdr*>(shard);
     unsigned long long* oe = reinterpret_cast<unsigned long long*>(shard + sizeof(RecHdr));
@@ -2060,22 +2129,28 @@ struct Shape {
 };
 
 // Segments per row and CTAs for a batch. A row is cut into at least enough segments of at most
-// SEG_BYTES, and into more (down to 2048 tokens) when the batch has fewer rows than the device
-// has resident CTAs. The grid takes min(segments, ctas) CTAs, which share the row-major list of
-// segments in equal contiguous ranges: every CTA streams the same number of bytes.
+// SEG_BYTES. When the batch has fewer rows than the device has resident CTAs, each row is cut
+// into c = ctas / B runs of whole segments (nseg a multiple of c, segments of at least 2048
+// tokens), so every CTA streams one run; with as many rows as CTAs or more, the CTAs share the
+// row-major list of segments in equal contiguous ranges. One run per CTA pays the per-run
+// set-up once and leaves SM room for the finishing kernel to start early.
 Shape plan(int64_t B, int64_t V, int dtype, int ctas) {
   const int es = dtype == VINFER_DTYPE_BF16 ? 2 : 4;
   const int A = 16 / es;
   const int64_t min_seg = (V * es + SEG_BYTES - 1) / SEG_BYTES;
-  int64_t want = std::min<int64_t>(std::min<int64_t>(MAX_NSEG, ctas / B), V / 2048);
-  int64_t nseg = std::max<int64_t>(min_seg, want);
+  int64_t c = 1;
+  if (B < ctas) c = std::min<int64_t>(ctas / B, MAX_NSEG);
+  c = std::max<int64_t>(1, std::min<int64_t>(c, V / 2048));
+  int64_t nseg = std::max<int64_t>(min_seg, c);
+  nseg = (nseg + c - 1) / c * c;
+  nseg = std::min<int64_t>(nseg, MAX_NSEG);
   int64_t len = (V + nseg - 1) / nseg;
   len = (len + A - 1) / A * A;
   nseg = (V + len - 1) / len;
   Shape s;
   s.nseg = (int)nseg;
   s.seg_len = (int)len;
-  s.grid = (int)std::min<int64_t>(B * nseg, ctas);
+  s.grid = (int)std::min<int64_t>(B * nseg, B < ctas ? B * c : ctas);
   return s;
 }
 
@@ -2085,10 +2160,11 @@ size_t align_up(size_t x) { return (x + ALIGN - 1) / ALIGN * ALIGN; }
 struct WsLayout {
   size_t counters, rows, recs, total;
 };
-// Records: one slot per (row, run); a row has at most nseg runs. The plan's nseg never
-// decreases with the CTA count, so the plan at the CTA cap bounds every device.
+// Records: one slot per (row, run); a row has at most nseg runs. Below the resident-CTA bound
+// rows may be split up to MAX_NSEG ways, depending on the device; from it on, the segment size
+// alone sets nseg. Either way the size does not depend on the device.
 WsLayout ws_layout(int64_t B, int64_t V, int dtype) {
-  const int64_t nseg = plan(B, V, dtype, CTA_CAP).nseg;
+  const int64_t nseg = B < CTA_CAP ? MAX_NSEG : plan(B, V, dtype, CTA_CAP).nseg;
   WsLayout L;
   L.counters = 0;
   L.rows = align_up((size_t)B * sizeof(int));
