@@ -127,7 +127,7 @@ int vinfer_sample_merge(const VinferSampleArgs* args, int32_t record_cap, const 
  * fixed array of VINFER_STATIC_SCRATCH_BYTES compiled into the library, which every device
  * that loads the library holds until the process exits. It allocates nothing.
  *  - Limit: the call returns VINFER_E_LIMIT when vinfer_sampler_workspace_bytes(batch, vocab,
- *    dtype) exceeds VINFER_STATIC_SCRATCH_BYTES (up to 63 rows fit at any vocabulary).
+ *    dtype) exceeds VINFER_STATIC_SCRATCH_BYTES (at least 63 rows fit at any vocabulary).
  *  - The first call on a device looks up the array's device address on that device (which
  *    may load the library's device code); make it before any stream capture.
  *  - All calls on one device share the array: calls that can overlap on the GPU (different
