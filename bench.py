@@ -35,6 +35,15 @@ import torch
 
 ROOT = Path(__file__).resolve().parent
 L2_BYTES = 126 * 1024 * 1024
+METRIC = "sampled rows/sec (logits HBM GB/s as % of B200 peak in roofline)"
+CONFIG3_WORKLOAD = ("config3: batch 256 x vocab 151936 bf16, rep 1.1 / pres 0.5 / freq 0.3 over "
+                    "4096-token Zipf(1.1) histories, temp 0.7, top-k 20, top-p 0.8")
+
+
+def config4_workload(world: int) -> str:
+    return ("config4: batch 1024 x vocab 248320 bf16 N(0,3) + 4 spikes, vocab-sharded over "
+            f"{world} GPUs, local top-k 50 records, NCCL all-gather, merge on every rank, temp 1, "
+            "top-k 50, top-p 0.9")
 SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -274,7 +283,7 @@ def bench_single(args) -> dict:
     cpu = None if args.no_cpu_baseline else cpu_reference_rows_per_s(w, args.cpu_seconds)
     ms_step = total_ms / K
     return {
-        "metric": "sampled rows/sec (logits HBM GB/s as % of B200 peak in roofline)",
+        "metric": METRIC,
         "value": B * K / (total_ms * 1e-3),
         "unit": "rows/s",
         "n_gpus": 1,
@@ -286,9 +295,7 @@ def bench_single(args) -> dict:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded, configuration 3)",
-        "config": {"workload": "config3: batch 256 x vocab 151936 bf16, rep 1.1 / pres 0.5 / "
-                               "freq 0.3 over 4096-token Zipf(1.1) histories, temp 0.7, "
-                               "top-k 20, top-p 0.8",
+        "config": {"workload": CONFIG3_WORKLOAD,
                    "batch": B, "vocab": V, "hist_nnz": w.hist_nnz,
                    "l2": f"{nbuf} rotating logits buffers "
                          f"({nbuf * w.logits.numel() * 2 / 2**20:.0f} MiB > 2x L2)",
@@ -420,7 +427,7 @@ def bench_sharded(args) -> dict | None:
     shard_algo = B * (hi - lo) * 2 + 36 * B  # local-record pass: this rank's logits and params
     achieved = shard_algo / (local_ms * 1e-3) / 1e9
     return {
-        "metric": "sampled rows/sec (logits HBM GB/s as % of B200 peak in roofline)",
+        "metric": METRIC,
         "value": B * args.steps / (ms * 1e-3),
         "unit": "rows/s",
         "n_gpus": world,
@@ -432,9 +439,7 @@ def bench_sharded(args) -> dict | None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded on the device, configuration 4 distribution)",
-        "config": {"workload": "config4: batch 1024 x vocab 248320 bf16 N(0,3) + 4 spikes, "
-                               f"vocab-sharded over {world} GPUs, local top-k 50 records, NCCL "
-                               "all-gather, merge on every rank, temp 1, top-k 50, top-p 0.9",
+        "config": {"workload": config4_workload(world),
                    "batch": B, "vocab": V, "shard_vocab": hi - lo,
                    "record_bytes_per_row": sampler.rec_bytes,
                    "allgather_bytes_per_rank": B * sampler.rec_bytes,
@@ -476,7 +481,7 @@ def bench_reference(args, world: int) -> dict:
     value = res["value"]
     return {
         "impl": "reference",
-        "metric": "sampled rows/sec (logits HBM GB/s as % of B200 peak in roofline)",
+        "metric": METRIC,
         "value": value,
         "unit": "rows/s",
         "n_gpus": world,
@@ -488,9 +493,10 @@ def bench_reference(args, world: int) -> dict:
         "vs_baseline": None,
         "dtype": "f32",
         "data": f"synthetic (seeded, configuration {config})",
-        "config": {"workload": f"config{config}" + ("" if config == 3 else " rows (batch 64 "
-                                                                            "sample, unsharded)"),
-                   "rows_per_step": rows_per_step},
+        "config": {"workload": CONFIG3_WORKLOAD if config == 3 else config4_workload(world),
+                   "rows_per_step": rows_per_step,
+                   "note": "each step samples rows_per_step rows of the configuration on the CPU "
+                           "(the whole row, unsharded); the metric is rows per second"},
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": res["cores"], "kind": "port",
                          "sample": res["sample"]},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0,

@@ -209,3 +209,82 @@ def test_host_side_argument_errors_do_not_launch(backend):
     with pytest.raises(ValueError):
         backend.sample_batch(x, params, torch.zeros(2, device=backend.device))
     assert _lib.load().vinfer_sample(None, None, 0, None) == _lib.E_ARG
+
+
+def _hist_csr(rows):
+    ptr, ids_, cnt = [0], [], []
+    for t in rows:
+        u, c = np.unique(np.asarray(t, np.int64), return_counts=True)
+        ids_.append(u.astype(np.int32))
+        cnt.append(c.astype(np.int32))
+        ptr.append(ptr[-1] + len(u))
+    return np.array(ptr, np.int64), np.concatenate(ids_), np.concatenate(cnt)
+
+
+def test_large_batch_rows_split_across_ctas(backend):
+    # more rows than resident CTAs: CTAs take equal ranges of segments, so rows end up split
+    # across runs in every way (records merged by the finishing kernel)
+    w = make(2, batch=600, vocab=20_000)
+    ids, probs = run_b200(backend, w, probs=False)
+    rows = list(range(0, 600, 7))
+    rep = compare(w, ids, None, rows=rows)
+    assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+def test_long_histories_beyond_the_staging_areas(backend):
+    # 3,000 and 5,000 distinct history ids: beyond the finishing kernel's staging (exact
+    # search) and, for the second, beyond the streaming kernel's (global-memory lookups)
+    V = 40_000
+    g = torch.Generator().manual_seed(11)
+    params = [dict(temperature=0.8, top_k=20, top_p=0.9, repetition_penalty=1.2,
+                   presence_penalty=0.3, frequency_penalty=0.1),
+              dict(temperature=1.0, top_k=0, top_p=0.8, repetition_penalty=0.9,
+                   presence_penalty=-0.2, frequency_penalty=0.05),
+              dict(temperature=0.0, repetition_penalty=1.5)]
+    x = (torch.randn(len(params), V, generator=g) * 2.0).to(torch.bfloat16)
+    rng = np.random.default_rng(2)
+    rows = [rng.choice(V, 3000, replace=False), rng.choice(V, 5000, replace=False),
+            rng.choice(V, 4500, replace=False)]
+    w = _workload(x, params, hist=_hist_csr(rows))
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+def test_small_batch_split_many_ways_with_penalties(backend):
+    # four rows over the whole device: each row is cut into dozens of runs
+    w = make(3, batch=4)
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+@pytest.mark.parametrize("k", [32, 33, 64, 192, 193])
+def test_top_k_around_the_candidate_path_limits(backend, k):
+    V = 30_000
+    g = torch.Generator().manual_seed(k)
+    params = [dict(temperature=0.9, top_k=k), dict(temperature=1.2, top_k=k, top_p=0.7),
+              dict(temperature=0.5, top_k=k, min_p=0.02)]
+    x = (torch.randn(len(params), V, generator=g) * 1.5).float()
+    w = _workload(x, params, seed=k)
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+def test_penalised_rows_without_top_k(backend):
+    # the online softmax sum corrected for penalised tokens (raw terms out, exact terms in)
+    V = 50_000
+    g = torch.Generator().manual_seed(5)
+    params = [dict(temperature=t, top_p=p, repetition_penalty=1.3, presence_penalty=0.7,
+                   frequency_penalty=0.2) for t, p in ((0.7, 0.9), (1.0, 0.5), (1.5, 0.95))]
+    x = (torch.randn(len(params), V, generator=g) * 2.5).to(torch.bfloat16)
+    rng = np.random.default_rng(6)
+    rows = []
+    for r in range(len(params)):
+        top = torch.topk(x[r].float(), 200).indices.numpy()  # penalise the likely tokens
+        rows.append(np.concatenate([top, rng.integers(0, V, 500)]))
+    w = _workload(x, params, hist=_hist_csr(rows))
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    assert not rep.failures, (str(rep), rep.failures[:5])
