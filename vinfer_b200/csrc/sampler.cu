@@ -52,7 +52,6 @@ constexpr int U = 8;                    // 16-byte vectors a thread loads per se
 constexpr int SEG_BYTES = NT * U * 16;  // 32 KiB: one round of loads of the CTA
 constexpr int CAND_BUF = 2048;          // candidates held for the run being processed
 constexpr int SCRATCH = 4096;           // 8-byte words of the scratch region (32 KiB)
-constexpr int HIST_CAP = SCRATCH;       // history entries of a run staged in scratch
 constexpr int CAND_CAP = 1024;          // entries of one record
 constexpr int KMAX = 192;               // largest top-k served by the candidate path
 constexpr int KC = 64;                  // candidates kept per run when top-k is off
@@ -67,6 +66,7 @@ static_assert(NT == 256, "block helpers assume 256 threads");
 static_assert(KMAX <= NCW * 32, "warp extraction covers at most 8 x 32 values");
 static_assert(KC <= 64, "block tightening ranks 64 delegates");
 static_assert(MERGE_CAP <= CAND_BUF && MERGE_CAP <= SCRATCH, "merge input and output fit");
+static_assert(SCRATCH * 64 >= VINFER_MAX_VOCAB, "a row's penalised-id bitmap fits scratch");
 static_assert((int64_t)VINFER_MAX_VOCAB * 4 <= (int64_t)MAX_NSEG * SEG_BYTES,
               "the largest float32 row fits MAX_NSEG segments");
 static_assert((CAND_BUF * 2 + SCRATCH * 2) * 32 >= VINFER_MAX_VOCAB,
@@ -1238,27 +1238,19 @@ __device__ int select_inplace(unsigned long long* buf, int n, int K, uint32_t* t
   return n >= K ? count_ge(buf, n, t) : n;
 }
 
-// the run's view of the row's history: the entries whose ids fall inside the run, in shared
-// memory (ids, then counts) when they fit, else read from global memory
+// The streaming kernel's view of a row's history: a bitmap, in shared memory, of the ids of this
+// shard (bit i = global id voff + i) that have a positive count, i.e. the penalised tokens.
 struct RunHist {
-  const int* ids;
-  const int* cnt;
-  int n;
-  bool shared;
+  const uint32_t* bits;
+  int64_t voff;
 };
-// the run's history view, as run() staged it (Smem::hpos, SC_NH, the table in scratch)
 __device__ __forceinline__ RunHist hist_view(const KParams& P, Smem& S) {
-  RunHist h;
-  h.n = S.sc[SC_NH];
-  h.shared = h.n <= HIST_CAP;
-  if (h.shared) {
-    h.ids = reinterpret_cast<const int*>(S.scratch);
-    h.cnt = h.ids + HIST_CAP;
-  } else {
-    h.ids = P.hids + S.hpos;
-    h.cnt = P.hcnt + S.hpos;
-  }
-  return h;
+  return RunHist{reinterpret_cast<const uint32_t*>(S.scratch), P.voff};
+}
+// is `id` a penalised token?
+__device__ __forceinline__ int hist_count(const RunHist& h, int id) {
+  const int i = (int)(id - h.voff);
+  return (h.bits[i >> 5] >> (i & 31)) & 1u;
 }
 
 // ---- delegates --------------------------------------------------------------------------------
@@ -1278,17 +1270,13 @@ __device__ __forceinline__ float dele_max(unsigned long long d) {
   return from_okey(~(uint32_t)(d >> 32));
 }
 
-// does an id of the run's history fall in [id0, id0 + n)?
+// is any of the ids [id0, id0 + n) a penalised token? (n <= 32)
 __device__ __forceinline__ bool hist_any(const RunHist& h, int id0, int n) {
-  int a = 0, b = h.n;
-  while (a < b) {
-    const int mid = (a + b) >> 1;
-    const int v = h.shared ? h.ids[mid] : __ldg(h.ids + mid);
-    if (v < id0) a = mid + 1; else b = mid;
-  }
-  if (a >= h.n) return false;
-  const int v = h.shared ? h.ids[a] : __ldg(h.ids + a);
-  return v < id0 + n;
+  const int i = (int)(id0 - h.voff);
+  const int w = i >> 5, b = i & 31;
+  const uint64_t two = (uint64_t)h.bits[w] | ((b + n > 32) ? (uint64_t)h.bits[w + 1] << 32 : 0ull);
+  const uint64_t mask = ((n >= 64) ? ~0ull : ((1ull << n) - 1ull)) << b;
+  return (two & mask) != 0ull;
 }
 
 // Note one delegate in the run's list (any lane). Returns its slot; slots past the list are
@@ -1504,10 +1492,10 @@ __device__ __forceinline__ void warp_first_bound(const KParams& P, const SegLoad
 // k_stream: every row streamed once; each run leaves an unsorted candidate record
 // ---------------------------------------------------------------------------------------------
 // A run record (global workspace, one slot per row and run): the run's threshold on raw logits,
-// its delegates (unsorted; every vector of the run holding a non-penalised element at or above
-// the threshold has one), and for rows without top-k its maximum raw logit and the softmax sum
-// of its raw logits relative to it. Greedy rows without penalties keep one entry instead: the
-// run's smallest composite key.
+// its candidates (unsorted composite keys of every non-penalised element at or above the
+// threshold), and for rows without top-k its maximum raw logit and the softmax sum of its raw
+// logits relative to it. Greedy rows without penalties keep one entry instead: the run's
+// smallest composite key.
 struct RunRec {
   float m;           // largest raw logit of the run (rows without top-k)
   float s;           // sum of exp2((y - m) * log2(e) / T) over the run's raw logits
@@ -1636,18 +1624,26 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
   // ---- the history entries inside this run's ids, staged in shared memory
   if (tid == 0) S.sc[SC_NH] = 0;
   if (pen && active) {
-    // the row's whole history (lookups only ever ask for ids of this run)
+    // a bitmap of the row's penalised ids of this shard (lookups: one shared-memory load)
+    uint32_t* bm = reinterpret_cast<uint32_t*>(S.scratch);
+    const int words = (int)((P.V + 31) / 32);
+    for (int i = tid; i < words; i += NT) bm[i] = 0u;
     const int64_t ia = __ldg(P.hrow + row);
     const int nh = (int)(__ldg(P.hrow + row + 1) - ia);
-    if (tid == 0) {
-      S.hpos = ia;
-      S.sc[SC_NH] = nh;
-    }
-    if (nh <= HIST_CAP) {
-      int* hid = reinterpret_cast<int*>(S.scratch);
-      for (int j = tid; j < nh; j += NT) {
-        hid[j] = __ldg(P.hids + ia + j);
-        hid[HIST_CAP + j] = __ldg(P.hcnt + ia + j);
+    cbar();
+    constexpr int PB = 8;  // entries per thread fetched together
+    for (int j0 = 0; j0 < nh; j0 += PB * NT) {
+      int id[PB], cn[PB];
+#pragma unroll
+      for (int k = 0; k < PB; ++k) {
+        const int j = j0 + k * NT + tid;
+        id[k] = j < nh ? __ldg(P.hids + ia + j) : 0;
+        cn[k] = j < nh ? __ldg(P.hcnt + ia + j) : 0;
+      }
+#pragma unroll
+      for (int k = 0; k < PB; ++k) {
+        const int64_t li = (int64_t)id[k] - P.voff;
+        if (cn[k] > 0 && li >= 0 && li < P.V) atomicOr(&bm[li >> 5], 1u << (li & 31));
       }
     }
   }
@@ -1702,14 +1698,33 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
   } else if (S.sc[SC_NC] > CAND_BUF) {
     flags |= REC_OVERFLOW;  // ties of the threshold flooded the list: exact search
   } else {
-    // only the delegates at or above the final threshold can hold a candidate
+    // the delegates at or above the final threshold are read again (just streamed, so from
+    // cache) and every non-penalised element at or above it is a candidate
+    using E = Elem<TIn>;
     const float ylo = from_okey(S.ylo_key);
     const int nd = S.sc[SC_NC];
+    const TIn* rowp = (const TIn*)P.logits + (int64_t)row * P.ld;
+    const RunHist h = hist_view(P, S);
+    RowCfg cq{};
+    cq.T = T;
+    cq.greedy = greedy;
+    auto emit = [&](float y, int id) {
+      if (!(y >= ylo)) return;
+      if (pen && hist_count(h, id) > 0) return;
+      const int pos = atomicAdd(&S.sc[SC_NRET], 1);
+      if (pos < CAND_CAP) ent[pos] = comp(okey(vf(y, cq)), id);
+    };
     for (int i = tid; i < nd; i += NT) {
       const unsigned long long x = S.cand[i];
-      if (dele_max(x) >= ylo) {
-        const int pos = atomicAdd(&S.sc[SC_NRET], 1);
-        if (pos < CAND_CAP) ent[pos] = x;
+      if (!(dele_max(x) >= ylo)) continue;
+      const int id0 = (int)((uint32_t)x & DL_ID);
+      const int64_t li = (int64_t)id0 - P.voff;
+      if ((uint32_t)x & DL_ONE) {
+        emit(E::ld(rowp, li), id0);
+      } else {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(rowp + li));
+#pragma unroll
+        for (int e = 0; e < E::A; ++e) emit(E::at(q, e), id0 + e);
       }
     }
     cbar();
@@ -1755,15 +1770,6 @@ __global__ void __launch_bounds__(NT, 3) k_stream(const KParams P) {
 // rank's shard record), falling back to the exact search when the candidates cannot decide the
 // row
 // ---------------------------------------------------------------------------------------------
-// is `id` a penalised token of the row (present in the staged history with a positive count)?
-__device__ __forceinline__ bool hist_pen(const int* ids, const float* tv, int n, int id) {
-  int a = 0, b = n;
-  while (a < b) {
-    const int mid = (a + b) >> 1;
-    if (ids[mid] < id) a = mid + 1; else b = mid;
-  }
-  return a < n && ids[a] == id && tv[a] == tv[a];  // NaN marks a count <= 0
-}
 
 template <typename TIn>
 __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
@@ -1910,48 +1916,27 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
   };
   bool sorted_done = false;  // the candidates are sorted and cut (short-list path)
   if (!exact) {
-    // ---- the runs' delegates (or greedy entries); each run kept only those at or above its
-    //      final threshold
+    // ---- the runs' candidates (or greedy entries)
     for (int idx = tid; idx < ntot; idx += NT) {
       int r = 0;
       while (S.moff[r + 1] <= idx) ++r;
       const unsigned long long* re = reinterpret_cast<const unsigned long long*>(
           base + (size_t)r * REC_STRIDE + sizeof(RunRec));
-      S.cand[idx] = __ldcg(re + (idx - S.moff[r]));
+      cand[idx] = __ldcg(re + (idx - S.moff[r]));
     }
+    if (tid == 0) S.sc[SC_NC] = ntot;
     cbar();
     if (greedy_plain) {
       // one entry per run: the smallest composite key is the first index of the maximum
       unsigned long long b = ~0ull;
-      for (int i = 0; i < ntot; ++i) b = S.cand[i] < b ? S.cand[i] : b;
+      for (int i = 0; i < ntot; ++i) b = cand[i] < b ? cand[i] : b;
+      cbar();
       if (tid == 0) cand[0] = b;
       nret = b != ~0ull;
       rflags = (nret && P.V > 1) ? REC_UNRETAINED : 0u;
       dkey = nret ? comp_key(b) : 0u;
       cbar();
     } else {
-      // ---- expansion: the delegates are read again and every non-penalised element at or
-      //      above its run's threshold becomes a candidate
-      auto emit = [&](float y, int id, float ylo) {
-        if (!(y >= ylo)) return;
-        if (c.pen && hist_pen(hid, htv, nh, id)) return;
-        const int pos = atomicAdd(&S.sc[SC_NC], 1);
-        if (pos < FCAP) cand[pos] = comp(okey(vf(y, cq)), id);
-      };
-      for (int idx = tid; idx < ntot; idx += NT) {
-        const unsigned long long x = S.cand[idx];
-        const int id0 = (int)((uint32_t)x & DL_ID);
-        const float ylo = from_okey(rh[run_of(id0)].ylo_key);
-        if (!(dele_max(x) >= ylo)) continue;
-        const int64_t li = (int64_t)id0 - P.voff;
-        if ((uint32_t)x & DL_ONE) {
-          emit(E::ld(rowp, li), id0, ylo);
-        } else {
-          const uint4 q = __ldg(reinterpret_cast<const uint4*>(rowp + li));
-#pragma unroll
-          for (int e = 0; e < E::A; ++e) emit(E::at(q, e), id0 + e, ylo);
-        }
-      }
       // ---- the penalised tokens with their exact values (computed before the wait)
       if (c.pen) {
         for (int j = tid; j < nh; j += NT) {
