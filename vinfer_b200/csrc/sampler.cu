@@ -1799,8 +1799,11 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
   if (tid == 0) S.sc[SC_NH] = 0;
   if (c.pen && tid < 32) {  // the row's history entries inside this shard
     const int64_t a = __ldg(P.hrow + row), b = __ldg(P.hrow + row + 1);
-    const int64_t ia = warp_lower_bound(P.hids, a, b, P.voff, lane);
-    const int64_t ib = warp_lower_bound(P.hids, ia, b, P.voff + P.V, lane);
+    int64_t ia = a, ib = b;
+    if (P.voff != 0 || P.V != P.vtotal) {  // a shard: search its part of the row
+      ia = warp_lower_bound(P.hids, a, b, P.voff, lane);
+      ib = warp_lower_bound(P.hids, ia, b, P.voff + P.V, lane);
+    }
     if (lane == 0) {
       S.hpos = ia;
       S.sc[SC_NH] = (int)(ib - ia);
@@ -1824,8 +1827,11 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
         cn[k] = j < nh ? __ldg(P.hcnt + S.hpos + j) : 0;
       }
 #pragma unroll
-      for (int k = 0; k < PB; ++k)
-        raw[k] = cn[k] > 0 ? E::ld(rowp, (int64_t)id[k] - P.voff) : 0.f;
+      for (int k = 0; k < PB; ++k) {
+        const int64_t li = (int64_t)id[k] - P.voff;
+        if (li < 0 || li >= P.V) cn[k] = 0;  // not a token of this shard (or of the vocabulary)
+        raw[k] = cn[k] > 0 ? E::ld(rowp, li) : 0.f;
+      }
 #pragma unroll
       for (int k = 0; k < PB; ++k) {
         const int j = j0 + k * NT + tid;
