@@ -1699,7 +1699,8 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
     flags |= REC_OVERFLOW;  // ties of the threshold flooded the list: exact search
   } else {
     // the delegates at or above the final threshold are read again (just streamed, so from
-    // cache) and every non-penalised element at or above it is a candidate
+    // cache) and every non-penalised element at or above it is a candidate; then the penalised
+    // tokens of top-k rows with their exact values
     using E = Elem<TIn>;
     const float ylo = from_okey(S.ylo_key);
     const int nd = S.sc[SC_NC];
@@ -1725,6 +1726,44 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
         const uint4 q = __ldg(reinterpret_cast<const uint4*>(rowp + li));
 #pragma unroll
         for (int e = 0; e < E::A; ++e) emit(E::at(q, e), id0 + e);
+      }
+    }
+    if (pen && !need_sum) {
+      // the penalised tokens of this run's ids at or above the threshold, with their exact
+      // values (their logits were just streamed, so from cache). Rows without top-k leave them
+      // to the finishing kernel, which also corrects the softmax sum with them.
+      RowCfg cp{};  // what penalize() needs
+      cp.rep = load_param(P, row, 3);
+      cp.pres = load_param(P, row, 4);
+      cp.freq = load_param(P, row, 5);
+      const int64_t ia = __ldg(P.hrow + row);
+      const int nh = (int)(__ldg(P.hrow + row + 1) - ia);
+      const int64_t idlo = P.voff + (int64_t)seg_a * P.seg_len;
+      const int64_t idhi = P.voff + min(P.V, (int64_t)(seg_b + 1) * P.seg_len);
+      constexpr int PB = 8;  // entries per thread fetched together
+      for (int j0 = 0; j0 < nh; j0 += PB * NT) {
+        int id[PB], cn[PB];
+        float raw[PB];
+#pragma unroll
+        for (int k = 0; k < PB; ++k) {
+          const int j = j0 + k * NT + tid;
+          id[k] = j < nh ? __ldg(P.hids + ia + j) : 0;
+          cn[k] = j < nh ? __ldg(P.hcnt + ia + j) : 0;
+        }
+#pragma unroll
+        for (int k = 0; k < PB; ++k) {
+          if (id[k] < idlo || id[k] >= idhi) cn[k] = 0;  // another run's, or outside the shard
+          raw[k] = cn[k] > 0 ? E::ld(rowp, (int64_t)id[k] - P.voff) : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < PB; ++k) {
+          if (cn[k] <= 0) continue;
+          const float yt = penalize(raw[k], cn[k], cp);
+          if (yt >= ylo) {
+            const int pos = atomicAdd(&S.sc[SC_NRET], 1);
+            if (pos < CAND_CAP) ent[pos] = comp(okey(vf(yt, cq)), id[k]);
+          }
+        }
       }
     }
     cbar();
@@ -1797,7 +1836,10 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
     S.rhi[tid] = (int)(P.voff + min(P.V, (int64_t)se * P.seg_len));
   }
   if (tid == 0) S.sc[SC_NH] = 0;
-  if (c.pen && tid < 32) {  // the row's history entries inside this shard
+  // rows with top-k (and greedy rows) find their penalised tokens in the run records; rows
+  // without top-k stage the history here to correct the softmax sum
+  const bool hist_here = c.pen && c.need_sum;
+  if (hist_here && tid < 32) {  // the row's history entries inside this shard
     const int64_t a = __ldg(P.hrow + row), b = __ldg(P.hrow + row + 1);
     int64_t ia = a, ib = b;
     if (P.voff != 0 || P.V != P.vtotal) {  // a shard: search its part of the row
@@ -1815,7 +1857,7 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
   const int nh = S.sc[SC_NH];
   const bool hshared = nh <= FCAP;
   // ---- the penalised values of the history entries: inputs only, so before the wait
-  if (c.pen && hshared) {
+  if (hist_here && hshared) {
     constexpr int PB = 8;  // entries per thread whose ids and logits are fetched together
     for (int j0 = 0; j0 < nh; j0 += PB * NT) {
       int id[PB], cn[PB];
@@ -1908,7 +1950,7 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
   }
   // with more history entries than the staging area holds, the row takes the exact search
   bool exact = (flags & (REC_EXACT | REC_OVERFLOW)) != 0 || ntot > CAND_BUF ||
-               (c.pen && !hshared);
+               (hist_here && !hshared);
   int nret = 0;
   uint32_t dkey = 0, rflags = 0;
   RowCfg cq{};  // what vf() needs
@@ -1944,7 +1986,7 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
       cbar();
     } else {
       // ---- the penalised tokens with their exact values (computed before the wait)
-      if (c.pen) {
+      if (hist_here) {
         for (int j = tid; j < nh; j += NT) {
           const float yt = htv[j];
           if (!(yt == yt)) continue;
