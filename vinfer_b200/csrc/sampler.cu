@@ -1630,6 +1630,10 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
     for (int i = tid; i < words; i += NT) bm[i] = 0u;
     const int64_t ia = __ldg(P.hrow + row);
     const int nh = (int)(__ldg(P.hrow + row + 1) - ia);
+    if (tid == 0) {  // for the penalised candidates at the end of the run
+      S.hpos = ia;
+      S.sc[SC_NH] = nh;
+    }
     cbar();
     constexpr int PB = 8;  // entries per thread fetched together
     for (int j0 = 0; j0 < nh; j0 += PB * NT) {
@@ -1715,17 +1719,32 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
       const int pos = atomicAdd(&S.sc[SC_NRET], 1);
       if (pos < CAND_CAP) ent[pos] = comp(okey(vf(y, cq)), id);
     };
-    for (int i = tid; i < nd; i += NT) {
-      const unsigned long long x = S.cand[i];
-      if (!(dele_max(x) >= ylo)) continue;
-      const int id0 = (int)((uint32_t)x & DL_ID);
-      const int64_t li = (int64_t)id0 - P.voff;
-      if ((uint32_t)x & DL_ONE) {
-        emit(E::ld(rowp, li), id0);
-      } else {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(rowp + li));
+    constexpr int DB = 2;  // delegate vectors per thread in flight
+    for (int i0 = 0; i0 < nd; i0 += DB * NT) {
+      uint4 q[DB];
+      uint32_t xb[DB];
 #pragma unroll
-        for (int e = 0; e < E::A; ++e) emit(E::at(q, e), id0 + e);
+      for (int k = 0; k < DB; ++k) {
+        const int i = i0 + k * NT + tid;
+        const unsigned long long x = i < nd ? S.cand[i] : ~0ull;
+        xb[k] = (i < nd && dele_max(x) >= ylo) ? (uint32_t)x : ~0u;
+        q[k] = make_uint4(0u, 0u, 0u, 0u);
+        if (xb[k] != ~0u) {
+          const int64_t li = (int64_t)(xb[k] & DL_ID) - P.voff;
+          if (xb[k] & DL_ONE) q[k].x = __float_as_uint(E::ld(rowp, li));
+          else q[k] = __ldg(reinterpret_cast<const uint4*>(rowp + li));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < DB; ++k) {
+        if (xb[k] == ~0u) continue;
+        const int id0 = (int)(xb[k] & DL_ID);
+        if (xb[k] & DL_ONE) {
+          emit(__uint_as_float(q[k].x), id0);
+        } else {
+#pragma unroll
+          for (int e = 0; e < E::A; ++e) emit(E::at(q[k], e), id0 + e);
+        }
       }
     }
     if (pen && !need_sum) {
@@ -1736,8 +1755,8 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
       cp.rep = load_param(P, row, 3);
       cp.pres = load_param(P, row, 4);
       cp.freq = load_param(P, row, 5);
-      const int64_t ia = __ldg(P.hrow + row);
-      const int nh = (int)(__ldg(P.hrow + row + 1) - ia);
+      const int64_t ia = S.hpos;
+      const int nh = S.sc[SC_NH];
       const int64_t idlo = P.voff + (int64_t)seg_a * P.seg_len;
       const int64_t idhi = P.voff + min(P.V, (int64_t)(seg_b + 1) * P.seg_len);
       constexpr int PB = 8;  // entries per thread fetched together
@@ -1773,17 +1792,19 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
       n = 0;
     }
   }
+  // the record is complete: count it for the row (k_finish may be waiting on exactly this).
+  // The barrier orders every thread's entries before thread 0's fence, whose release
+  // covers them.
+  cbar();
   if (tid == 0) {
     hd->m = m;
     hd->s = sum;
     hd->ylo_key = S.ylo_key;
     hd->n = n;
     hd->flags = flags;
+    __threadfence();
+    atom_add_acq_rel(&P.counters[row], 1);
   }
-  // the record is complete: count it for the row (k_finish may be waiting on exactly this)
-  __threadfence();
-  cbar();
-  if (tid == 0) atom_add_acq_rel(&P.counters[row], 1);
 }
 
 template <typename TIn>
