@@ -217,6 +217,15 @@ struct Elem<float> {
     const uint32_t w = e == 0 ? q.x : e == 1 ? q.y : e == 2 ? q.z : q.w;
     return __uint_as_float(w);
   }
+  __device__ static float vmin(const uint4& q) {
+    return fminf(fminf(__uint_as_float(q.x), __uint_as_float(q.y)),
+                 fminf(__uint_as_float(q.z), __uint_as_float(q.w)));
+  }
+  // is any element a NaN with the sign bit clear? (bit patterns 0x7F800001 .. 0x7FFFFFFF)
+  __device__ static bool pos_nan(const uint4& q) {
+    return (q.x - 0x7F800001u) < 0x007FFFFFu || (q.y - 0x7F800001u) < 0x007FFFFFu ||
+           (q.z - 0x7F800001u) < 0x007FFFFFu || (q.w - 0x7F800001u) < 0x007FFFFFu;
+  }
 };
 template <>
 struct Elem<__nv_bfloat16> {
@@ -242,6 +251,23 @@ struct Elem<__nv_bfloat16> {
     const __nv_bfloat162 d = *reinterpret_cast<const __nv_bfloat162*>(&q.w);
     const __nv_bfloat162 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
     return fmaxf(__low2float(m), __high2float(m));
+  }
+  __device__ static float vmin(const uint4& q) {
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&q.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&q.y);
+    const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&q.z);
+    const __nv_bfloat162 d = *reinterpret_cast<const __nv_bfloat162*>(&q.w);
+    const __nv_bfloat162 m = __hmin2(__hmin2(a, b), __hmin2(c, d));
+    return fminf(__low2float(m), __high2float(m));
+  }
+  // is any element a NaN with the sign bit clear? (halves 0x7F81 .. 0x7FFF)
+  __device__ static bool pos_nan(const uint4& q) {
+    const uint32_t lo = 0x7F807F80u, hi = 0x80008000u;
+    const uint32_t r = (__vcmpgtu2(q.x, lo) & __vcmpltu2(q.x, hi)) |
+                       (__vcmpgtu2(q.y, lo) & __vcmpltu2(q.y, hi)) |
+                       (__vcmpgtu2(q.z, lo) & __vcmpltu2(q.z, hi)) |
+                       (__vcmpgtu2(q.w, lo) & __vcmpltu2(q.w, hi));
+    return r != 0u;
   }
   __device__ static float at(const uint4& q, int e) {
     const uint32_t w = (e >> 1) == 0 ? q.x : (e >> 1) == 1 ? q.y : (e >> 1) == 2 ? q.z : q.w;
@@ -771,6 +797,11 @@ struct RowBits {
   __device__ uint32_t& word(int w) const { return w < N0 ? w0[w] : w1[w - N0]; }
   __device__ bool bit(int i) const { return (word(i >> 5) >> (i & 31)) & 1u; }
 };
+// history entries staged for the exact search (second half of scratch): local index, key
+constexpr int XSTAGE = SCRATCH / 2;
+// a bin of the exact search holding at most this many elements is collected and sorted
+// (Smem::mh viewed as 8-byte entries)
+constexpr int XCOLLECT = (int)(sizeof(RecHdr) * MAX_NSEG / 8);
 
 template <typename TIn>
 struct ExactRow {
@@ -781,45 +812,215 @@ struct ExactRow {
   int64_t hist_a, hist_b;
   int V;
   float mv;
+  const int* sid;        // staged history entries, ascending local index ...
+  const uint32_t* skey;  // ... and the processed key of each penalised one
+  int ns;                // staged entries; -1 when they did not fit (searched in global memory)
 
-  __device__ float y_at(int i) const {
-    float x = Elem<TIn>::ld(rowp, i);
-    if (c.pen && bm.bit(i)) {
-      const int64_t p = lower_bound_ids(P.hids, hist_a, hist_b, P.voff + i);
-      x = penalize(x, __ldg(P.hcnt + p), c);
+  // processed key of penalised position i
+  __device__ uint32_t pen_key(int i) const {
+    if (ns >= 0) {
+      int lo = 0, hi = ns;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (sid[mid] < i) lo = mid + 1; else hi = mid;
+      }
+      return skey[lo];
     }
-    return x;
+    const int64_t p = lower_bound_ids(P.hids, hist_a, hist_b, P.voff + i);
+    return okey(vf(penalize(Elem<TIn>::ld(rowp, i), __ldg(P.hcnt + p), c), c));
   }
-  __device__ uint32_t key_at(int i) const { return okey(vf(y_at(i), c)); }
+  __device__ uint32_t key_at(int i) const {
+    if (c.pen && bm.bit(i)) return pen_key(i);
+    return okey(vf(Elem<TIn>::ld(rowp, i), c));
+  }
   __device__ unsigned long long wfx(uint32_t key) const {
     const float e = ex2((from_okey(key) - mv) * LOG2E);
-    return (unsigned long long)__float2ull_rn(e * (float)FX_ONE);
+    const unsigned long long w = (unsigned long long)__float2ull_rn(e * (float)FX_ONE);
+    return w <= (1ull << 44) ? w : (1ull << 44);  // e <= 1 (a NaN converts to anything)
   }
 };
 
-// Histogram update for one element per lane (`ok` lanes only). When every active lane of the
-// warp falls in the same bin, which is the common case on the coarse levels of a float radix,
-// the warp adds its totals once instead of contending 32 times on one address.
-__device__ __forceinline__ void warp_bin_add(bool ok, uint32_t b, unsigned long long mw,
-                                             uint32_t* cnt, unsigned long long* mass) {
-  const unsigned act = __ballot_sync(FULLMASK, ok);
-  if (!act) return;
-  const int lane = threadIdx.x & 31;
-  const int ldr = __ffs(act) - 1;
-  const uint32_t bl = __shfl_sync(FULLMASK, b, ldr);
-  if (__all_sync(FULLMASK, !ok || b == bl)) {
-    unsigned long long sum = mw;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(FULLMASK, sum, o);
-    if (lane == ldr) {
-      atomicAdd(&cnt[bl], (uint32_t)__popc(act));
-      if (mass) atomicAdd(&mass[bl], sum);
-    }
-  } else if (ok) {
-    atomicAdd(&cnt[b], 1u);
-    if (mass) atomicAdd(&mass[b], mw);
+// are any of the positions [i0, i0 + n) set in the bitmap? (n <= 32, i0 + n <= V)
+__device__ __forceinline__ bool bits_any(const RowBits& bm, int V, int i0, int n) {
+  const int w = i0 >> 5;
+  unsigned long long win = bm.word(w);
+  if (((i0 & 31) + n) > 32 && (w + 1) * 32 < V) win |= (unsigned long long)bm.word(w + 1) << 32;
+  return ((win >> (i0 & 31)) & ((1ull << n) - 1ull)) != 0ull;
+}
+// the first element of a vector, and the vector shifted down by one element
+template <typename TIn>
+__device__ __forceinline__ void shift_elem(uint4& q) {
+  constexpr int SB = 128 / Elem<TIn>::A;  // bits per element
+  if (SB == 32) {
+    q.x = q.y;
+    q.y = q.z;
+    q.z = q.w;
+  } else {
+    q.x = __funnelshift_r(q.x, q.y, SB);
+    q.y = __funnelshift_r(q.y, q.z, SB);
+    q.z = __funnelshift_r(q.z, q.w, SB);
+    q.w >>= SB;
   }
 }
+
+// Walks a row of V logits: vec(q, i0, valid) once per 16-byte vector slot of every thread
+// (whole warps call it together; i0 = position of the vector's first element), then
+// edge(valid, y, i) once per lane of warp 0 for the ragged head and tail (fewer than 32
+// positions, any alignment). Four vectors per thread are in flight; they are visited one per
+// iteration, rotated through registers, which keeps the loop body at one vector's worth of code.
+template <typename TIn, typename FV, typename FE>
+__device__ __forceinline__ void row_walk(const TIn* rowp, int V, FV&& vec, FE&& edge) {
+  using E = Elem<TIn>;
+  constexpr int A = E::A;
+  constexpr int UE = 4;
+  const int tid = threadIdx.x;
+  const uintptr_t addr = (uintptr_t)rowp;
+  int head = (int)(((16u - (uint32_t)(addr & 15u)) & 15u) / sizeof(TIn));
+  if (head > V) head = V;
+  const int nv = (V - head) / A;
+  const int tail0 = head + nv * A;
+  const uint4* vb = reinterpret_cast<const uint4*>(rowp + head);
+  for (int j0 = 0; j0 < nv; j0 += NT * UE) {
+    uint4 q0, q1, q2, q3;
+    {
+      const int j = j0 + tid;
+      q0 = j < nv ? __ldg(vb + j) : make_uint4(0u, 0u, 0u, 0u);
+      q1 = j + NT < nv ? __ldg(vb + j + NT) : make_uint4(0u, 0u, 0u, 0u);
+      q2 = j + 2 * NT < nv ? __ldg(vb + j + 2 * NT) : make_uint4(0u, 0u, 0u, 0u);
+      q3 = j + 3 * NT < nv ? __ldg(vb + j + 3 * NT) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll 1
+    for (int u = 0; u < UE; ++u) {
+      const int j = j0 + u * NT + tid;
+      vec(q0, head + j * A, j < nv);
+      q0 = q1;
+      q1 = q2;
+      q2 = q3;
+    }
+  }
+  if (tid < 32) {
+    const int nht = head + (V - tail0);
+    const bool valid = tid < nht;
+    const int i = tid < head ? tid : tail0 + (tid - head);
+    edge(valid, valid ? E::ld(rowp, i) : 0.f, i);
+  }
+}
+
+// Visits every position of the row once: f(ok, key, i), called by whole warps (f may use warp
+// collectives). A position is visited with its key and ok = true when it is penalised or when
+// its raw logit y satisfies !(y < ylo) && !(y >= ynext); otherwise with ok = false and no key
+// (the caller chose the interval so that such positions cannot hold a key it looks for, which
+// skips the division).
+template <typename TIn, typename F>
+__device__ __forceinline__ void row_pass(const ExactRow<TIn>& X, float ylo, float ynext, F&& f) {
+  using E = Elem<TIn>;
+  constexpr int A = E::A;
+  // everything the loop reads, in registers (X may live in memory)
+  const int V = X.V;
+  const bool pen = X.c.pen;
+  const RowBits bm = X.bm;
+  RowCfg cl{};  // what vf() needs
+  cl.T = X.c.T;
+  cl.greedy = X.c.greedy;
+  auto visit = [&](bool valid, bool maybe_pen, float y, int i) {
+    bool ok = false;
+    uint32_t key = 0;
+    if (valid) {
+      if (maybe_pen && bm.bit(i)) {
+        key = X.pen_key(i);
+        ok = true;
+      } else if (!(y < ylo) && !(y >= ynext)) {
+        key = okey(vf(y, cl));
+        ok = true;
+      }
+    }
+    f(ok, key, i);
+  };
+  row_walk<TIn>(
+      X.rowp, V,
+      [&](uint4 q, int i0, bool vv) {
+        const bool mp = vv && pen && bits_any(bm, V, i0, A);
+#pragma unroll 1
+        for (int e = 0; e < A; ++e) {
+          visit(vv, mp, E::at(q, 0), i0 + e);
+          shift_elem<TIn>(q);
+        }
+      },
+      [&](bool valid, float y, int i) { visit(valid, pen, y, i); });
+}
+
+// Calls f(key, i), lane by lane (f uses no warp collectives), for the positions that are
+// penalised or whose raw logit y satisfies !(y < ylo) && !(y >= ynext). Vectors whose
+// minimum and maximum rule out both are skipped whole, so a narrow interval costs little more
+// than reading the row.
+template <typename TIn, typename F>
+__device__ __forceinline__ void row_pass_sparse(const ExactRow<TIn>& X, float ylo, float ynext, F&& f) {
+  using E = Elem<TIn>;
+  constexpr int A = E::A;
+  const int V = X.V;
+  const bool pen = X.c.pen;
+  const RowBits bm = X.bm;
+  RowCfg cl{};
+  cl.T = X.c.T;
+  cl.greedy = X.c.greedy;
+  const bool open_hi = !(ynext == ynext);  // NaN: no upper bound
+  auto elem = [&](bool maybe_pen, float y, int i) {
+    if (maybe_pen && bm.bit(i)) f(X.pen_key(i), i);
+    else if (!(y < ylo) && !(y >= ynext)) f(okey(vf(y, cl)), i);
+  };
+  row_walk<TIn>(
+      X.rowp, V,
+      [&](uint4 q, int i0, bool vv) {
+        if (!vv) return;
+        const bool mp = pen && bits_any(bm, V, i0, A);
+        if (!mp && (E::vmax(q) < ylo || !(open_hi || E::vmin(q) < ynext))) return;
+#pragma unroll 1
+        for (int e = 0; e < A; ++e) {
+          elem(mp, E::at(q, 0), i0 + e);
+          shift_elem<TIn>(q);
+        }
+      },
+      [&](bool valid, float y, int i) {
+        if (valid) elem(pen, y, i);
+      });
+}
+
+// Radix bins of the exact search: element counts and fixed-point masses. 64-bit shared-memory
+// adds contend badly on the few hot bins of a float radix, so a mass (at most 2^44, 45 bits) is
+// added as four 12-bit parts to four 32-bit bins; a bin receives at most VINFER_MAX_VOCAB
+// = 2^18 elements, so no part sum overflows. All adds are lane by lane.
+static_assert(VINFER_MAX_VOCAB <= (1 << 18), "12-bit mass parts of a bin cannot overflow");
+static_assert(sizeof(RecHdr) * MAX_NSEG >= 2 * 256 * sizeof(uint32_t), "parts 2 and 3 fit Smem::mh");
+struct BinHist {
+  uint32_t* cnt;  // [256]
+  uint32_t* p01;  // mass parts 0 and 1: [2][256] (Smem::bin_mass)
+  uint32_t* p23;  // mass parts 2 and 3: [2][256] (Smem::mh)
+  __device__ explicit BinHist(Smem& S)
+      : cnt(S.bin_cnt), p01(reinterpret_cast<uint32_t*>(S.bin_mass)),
+        p23(reinterpret_cast<uint32_t*>(S.mh)) {}
+  __device__ void clear() const {  // by every thread of the CTA (NT == 256)
+    const int t = threadIdx.x;
+    cnt[t] = 0u;
+    p01[t] = 0u;
+    p01[256 + t] = 0u;
+    p23[t] = 0u;
+    p23[256 + t] = 0u;
+  }
+  __device__ void add(uint32_t b, bool with_mass, unsigned long long w) const {
+    atomicAdd(&cnt[b], 1u);
+    if (!with_mass) return;
+    const uint32_t q0 = (uint32_t)w & 0xFFFu, q1 = (uint32_t)(w >> 12) & 0xFFFu;
+    const uint32_t q2 = (uint32_t)(w >> 24) & 0xFFFu, q3 = (uint32_t)(w >> 36) & 0xFFFu;
+    if (q0) atomicAdd(&p01[b], q0);
+    if (q1) atomicAdd(&p01[256 + b], q1);
+    if (q2) atomicAdd(&p23[b], q2);
+    if (q3) atomicAdd(&p23[256 + b], q3);
+  }
+  __device__ unsigned long long mass(int b) const {
+    return (unsigned long long)p01[b] + ((unsigned long long)p01[256 + b] << 12) +
+           ((unsigned long long)p23[b] << 24) + ((unsigned long long)p23[256 + b] << 36);
+  }
+};
 
 // kept-set predicate of the exact search
 struct Cut {
@@ -835,80 +1036,238 @@ struct Cut {
   }
 };
 
-struct Found {
-  uint32_t w;                // key of the tie group reached
-  unsigned long long above;  // fixed-point mass strictly above w (kept elements)
-  int j;                     // 1-based rank inside the tie group, ascending id
-  int n_w;
+// One thread's bin of the first radix level (thread t holds bin 255 - t): returned by a search
+// (out) and, adjusted to a narrower cut, given to the next one (in) in place of its first pass.
+struct Level0 {
+  bool in;
+  int cut_bin;           // (in) the bin the narrower cut passes through: its count is unknown
+  unsigned long long m;  // weight of the bin
+  uint32_t c;            // elements in it
+  unsigned long long mo;
+  uint32_t co;
 };
 
-// Canonical position where the cumulative kept mass first reaches (>=) or passes (>) target:
-// four levels of 8-bit radix histograms of count and fixed-point mass over the keys.
+struct Found {
+  uint32_t w;                // key of the tie group reached
+  unsigned long long above;  // weight strictly above w (kept elements)
+  int j;                     // 1-based rank inside the tie group, ascending id
+  int n_w;
+  int id;                    // local index of the element, -1 when left to exact_jth
+};
+
+__device__ float ylo_for(float vt, const RowCfg& c);
+// Raw-logit interval [ylo, ynext) of the positions whose processed key lies in [klo, khi]
+// (vf is monotone): ylo is the smallest y with vf(y) >= from_okey(klo), ynext the smallest y
+// with vf(y) above from_okey(khi). Keys outside the finite range leave the bound open (NaN
+// upper bound: nothing compares >= it). Warp-wide (ylo_for).
+__device__ void raw_range(const RowCfg& c, uint32_t klo, uint32_t khi, float* ylo, float* ynext) {
+  const uint32_t kninf = okey(-INFINITY), kpinf = okey(INFINITY);
+  if (klo <= kninf) *ylo = -INFINITY;
+  else if (klo > kpinf) *ylo = INFINITY;
+  else *ylo = ylo_for(from_okey(klo), c);
+  if (khi >= kpinf) *ynext = __int_as_float(0x7fc00000);
+  else if (khi < kninf) *ynext = -INFINITY;
+  else *ynext = ylo_for(from_okey(khi + 1u == 0x7FFFFFFFu ? 0x80000000u : khi + 1u), c);
+}
+
+// Mass-scale bins, the first step of a mass search: bin of a key by d = (mv - v) log2(e) in
+// quarter units; bin 255 holds d >= 63.75 (and NaN), keys above the finite range count as bin 0.
+// Non-increasing in the key, so ascending bins are keys in descending order, and each bin holds
+// a narrow slice of the probability mass whatever the spread of the row.
+__device__ __forceinline__ int dbin(uint32_t key, float mv) {
+  if (key > 0xFF800000u) return 0;  // above +inf: a NaN with the sign bit clear
+  const float d = (mv - from_okey(key)) * LOG2E;
+  if (!(d < 63.75f)) return 255;
+  return d > 0.f ? (int)(d * 4.f) : 0;
+}
+// smallest key whose mass-scale bin is <= b (the bins are monotone in the key)
+__device__ uint32_t dbin_lowkey(int b, float mv) {
+  uint32_t lo = 0u, hi = 0xFFFFFFFFu;
+  while (lo < hi) {
+    const uint32_t mid = lo + (hi - lo) / 2u;
+    if (dbin(mid, mv) <= b) hi = mid; else lo = mid + 1u;
+  }
+  return lo;
+}
+
+// Canonical position where the cumulative kept weight first reaches (>=) or passes (>)
+// `target`: weight = fixed-point mass (mass_w) or 1. The search narrows a key interval known
+// to hold that position: for a mass search the first step bins by mass scale (dbin), then
+// 8-bit radix digits over the highest bits in which the interval's ends differ; once the
+// interval holds at most XCOLLECT kept elements they are collected and sorted, which resolves
+// the element itself. With frac >= 0 the target is frac x the total weight (the first step's
+// histogram gives the total, also returned). l0 carries the first step's bins out, or in
+// (adjusted to a narrower cut) in place of its pass.
 template <typename TIn>
-__device__ Found exact_search(const ExactRow<TIn>& X, const Cut& cut, unsigned long long target,
-                              bool strict, Smem& S) {
-  uint32_t* cnt = S.bin_cnt;
-  unsigned long long* mass = S.bin_mass;
+__device__ Found exact_search(const ExactRow<TIn>& X, const Cut& cut_in,
+                              unsigned long long target, double frac, bool strict, bool mass_w,
+                              Smem& S, unsigned long long* total_out, Level0* l0) {
+  const Cut cut = cut_in;  // in registers: the passes test it per element
+  const float mv = X.mv;
+  const BinHist hist(S);
+  unsigned long long* buf = reinterpret_cast<unsigned long long*>(S.mh);
   const int tid = threadIdx.x;
-  uint32_t prefix = 0;
-  unsigned long long above = 0;
-  int last_cnt = 0;
+  auto weight = [&](uint32_t key) -> unsigned long long {
+    if (!mass_w) return 1ull;
+    const float e = ex2((from_okey(key) - mv) * LOG2E);
+    const unsigned long long w = (unsigned long long)__float2ull_rn(e * (float)FX_ONE);
+    return w <= (1ull << 44) ? w : (1ull << 44);  // e <= 1 (a NaN converts to anything)
+  };
+  // no kept key lies below this (the prefilter's floor)
+  uint32_t klo = max(max(cut.tk, cut.mk), cut.kind == 0 ? cut.ck : 0u);
+  uint32_t khi = 0xFFFFFFFFu;
+  unsigned long long above = 0;  // kept weight above khi
+  int n_in = 0x7FFFFFFF;         // kept elements in [klo, khi] (not known before the first step)
 #pragma unroll 1
-  for (int lv = 0; lv < 4; ++lv) {
-    const int sh = 24 - 8 * lv;
-    cnt[tid] = 0;
-    mass[tid] = 0ull;
-    cbar();
-    for (int base = 0; base < X.V; base += NT) {
-      const int i = base + tid;
-      bool ok = i < X.V;
-      uint32_t key = 0;
-      if (ok) {
-        key = X.key_at(i);
-        ok = cut.keep(key, i) && (lv == 0 || (key >> (sh + 8)) == prefix);
+  for (int step = 0; step < 8; ++step) {
+    if (n_in <= XCOLLECT) {
+      // ---- collect the interval, sort it (canonical order) and walk its cumulative weight
+      float ylo, ynext;
+      raw_range(X.c, klo, khi, &ylo, &ynext);
+      if (tid == 0) S.sc[SC_NQ] = 0;
+      cbar();
+      row_pass_sparse(X, ylo, ynext, [&](uint32_t key, int i) {
+        if (key >= klo && key <= khi && cut.keep(key, i)) {
+          const int pos = atomicAdd(&S.sc[SC_NQ], 1);
+          if (pos < XCOLLECT) buf[pos] = comp(key, i);
+        }
+      });
+      cbar();
+      const int n = min(S.sc[SC_NQ], XCOLLECT);
+      if (n == 0) {
+        Found f = {0u, 0ull, 0, 0, -1};
+        return f;
       }
-      warp_bin_add(ok, (key >> sh) & 255u, ok ? X.wfx(key) : 0ull, cnt, mass);
+      unsigned long long x = tid < n ? buf[tid] : ~0ull;
+      int rank = 0;
+      if (tid < n)
+        for (int t = 0; t < n; ++t) rank += buf[t] < x;
+      cbar();
+      if (tid < n) buf[rank] = x;
+      cbar();
+      x = tid < n ? buf[tid] : ~0ull;
+      const uint32_t kx = comp_key(x);
+      const unsigned long long wx = tid < n ? weight(kx) : 0ull;
+      unsigned long long tot2;
+      const unsigned long long exw = cta_excl_scan_u64(wx, &tot2, S);
+      const unsigned long long bef = above + exw, aft = bef + wx;
+      const bool cr = tid < n && (strict ? (aft > target) : (aft >= target));
+      unsigned long long first = cta_min_u64(cr ? (unsigned long long)tid : ~0ull, S);
+      if (first == ~0ull) first = (unsigned long long)(n - 1);  // rounding: the last element
+      const uint32_t w = comp_key(buf[(int)first]);
+      // the tie group of w: its first index, size and the weight above it
+      const unsigned long long g0 =
+          cta_min_u64(tid < n && kx == w ? (unsigned long long)tid : ~0ull, S);
+      int ng;
+      cta_excl_scan_i(tid < n && kx == w ? 1 : 0, &ng, S);
+      if (tid == (int)g0) S.red64[NCW] = bef;
+      cbar();
+      Found f;
+      f.w = w;
+      f.above = S.red64[NCW];
+      f.n_w = ng;
+      const unsigned long long ew = weight(w);
+      long long j;
+      if (ew == 0) {
+        j = ng;
+      } else if (target < f.above) {
+        j = 1;
+      } else {
+        const unsigned long long d = target - f.above;
+        j = strict ? (long long)(d / ew) + 1 : (long long)((d + ew - 1) / ew);
+      }
+      if (j < 1) j = 1;
+      if (j > ng) j = ng;
+      f.j = (int)j;
+      f.id = comp_id(buf[(int)g0 + f.j - 1]);
+      cbar();
+      return f;
     }
-    cbar();
-    // thread t owns bin 255 - t, so thread order is descending key order
-    const int b = 255 - tid;
-    const unsigned long long mb = mass[b];
-    const uint32_t cb = cnt[b];
+    if (klo == khi) break;  // one key: a tie group too large to collect
+    // ---- one step: bins over [klo, khi]; thread t holds the bin at position t in descending
+    // key order
+    const bool dstep = step == 0 && mass_w;
+    int sh = 0;
+    uint32_t base = 0u;
+    if (!dstep) {
+      const int hb = 31 - __clz(klo ^ khi);
+      sh = hb >= 7 ? hb - 7 : 0;
+      base = klo >> sh;
+    }
+    unsigned long long mb;
+    uint32_t cb;
+    const bool given = step == 0 && l0 && l0->in;
+    if (given) {
+      mb = l0->m;
+      cb = l0->c;
+    } else {
+      float ylo, ynext;
+      raw_range(X.c, klo, khi, &ylo, &ynext);
+      hist.clear();
+      cbar();
+      row_pass_sparse(X, ylo, ynext, [&](uint32_t key, int i) {
+        if (key < klo || key > khi || !cut.keep(key, i)) return;
+        const int bi = dstep ? dbin(key, mv) : 255 - (int)((key >> sh) - base);
+        hist.add((uint32_t)bi, mass_w, mass_w ? weight(key) : 0ull);
+      });
+      cbar();
+      cb = hist.cnt[tid];
+      mb = mass_w ? hist.mass(tid) : (unsigned long long)cb;
+    }
+    if (step == 0 && l0) {
+      l0->mo = mb;
+      l0->co = cb;
+    }
     unsigned long long tot;
     const unsigned long long ex = cta_excl_scan_u64(mb, &tot, S);
+    if (step == 0) {
+      if (total_out) *total_out = tot;
+      if (frac >= 0.0) target = (unsigned long long)(frac * (double)tot);
+    }
     const unsigned long long before = above + ex, after = before + mb;
     const bool cross_after = strict ? (after > target) : (after >= target);
     const bool cross_before = strict ? (before > target) : (before >= target);
     unsigned long long pick = ~0ull;
     if (cb > 0 && cross_after && !cross_before) pick = (unsigned long long)tid;
     pick = cta_min_u64(pick, S);
-    if (pick == ~0ull) {  // target at or beyond the total (rounding): the lowest non-empty bin
+    if (pick == ~0ull) {  // target at or beyond the total (rounding): the last non-empty bin
       pick = cta_min_u64(cb > 0 ? (unsigned long long)(NT - 1 - tid) : ~0ull, S);
       if (pick == ~0ull) {
-        Found f = {0u, 0ull, 0, 0};
+        Found f = {0u, 0ull, 0, 0, -1};
         return f;
       }
       pick = (unsigned long long)(NT - 1 - (int)pick);
     }
     if ((int)pick == tid) {
-      S.sc[SC_B] = b;
       S.red64[NCW] = before;
-      S.sc[SC_J] = (int)cb;
+      S.sc[SC_J] = (given && tid == l0->cut_bin) ? 0x7FFFFFFF : (int)cb;
     }
     cbar();
-    prefix = (prefix << 8) | (uint32_t)S.sc[SC_B];
+    const int t = (int)pick;
+    uint32_t kl, kh;
+    if (dstep) {
+      kl = dbin_lowkey(t, mv);
+      kh = t == 0 ? 0xFFFFFFFFu : dbin_lowkey(t - 1, mv) - 1u;
+    } else {
+      kl = (base + (uint32_t)(255 - t)) << sh;
+      kh = kl | ((1u << sh) - 1u);
+    }
+    klo = max(klo, kl);
+    khi = min(khi, kh);
     above = S.red64[NCW];
-    last_cnt = S.sc[SC_J];
+    n_in = S.sc[SC_J];
     cbar();
   }
+  // a single key holding more than XCOLLECT kept elements: its j-th by index, found later
   Found f;
-  f.w = prefix;
+  f.w = klo;
   f.above = above;
-  f.n_w = last_cnt;
-  const unsigned long long ew = X.wfx(prefix);
+  f.n_w = n_in;
+  f.id = -1;
+  const unsigned long long ew = weight(klo);
   long long j;
   if (ew == 0) {
-    j = last_cnt;
+    j = n_in;
   } else if (target < above) {
     j = 1;
   } else {
@@ -916,7 +1275,7 @@ __device__ Found exact_search(const ExactRow<TIn>& X, const Cut& cut, unsigned l
     j = strict ? (long long)(d / ew) + 1 : (long long)((d + ew - 1) / ew);
   }
   if (j < 1) j = 1;
-  if (j > last_cnt) j = last_cnt;
+  if (j > n_in) j = n_in;
   f.j = (int)j;
   return f;
 }
@@ -952,13 +1311,21 @@ __device__ int exact_jth(const ExactRow<TIn>& X, const Cut& cut, uint32_t w, int
   }
   return -1;
 }
+template <typename TIn>
+__device__ int found_index(const ExactRow<TIn>& X, const Cut& cut, const Found& f, Smem& S) {
+  if (f.n_w <= 0) return -1;
+  return f.id >= 0 ? f.id : exact_jth(X, cut, f.w, f.j, S);
+}
 
 template <typename TIn>
 __device__ __noinline__ void exact_row(const KParams& P, const RowCfg& c, int row, Smem& S,
                                        unsigned char* scratch) {
   const int tid = threadIdx.x;
   const RowBits bm{(uint32_t*)S.cand, (uint32_t*)scratch};
-  ExactRow<TIn> X{P, c, bm, (const TIn*)P.logits + (int64_t)row * P.ld, 0, 0, (int)P.V, 0.f};
+  int* sid = reinterpret_cast<int*>(reinterpret_cast<unsigned long long*>(scratch) + XSTAGE);
+  uint32_t* skey = reinterpret_cast<uint32_t*>(sid + XSTAGE);
+  ExactRow<TIn> X{P, c, bm, (const TIn*)P.logits + (int64_t)row * P.ld, 0, 0, (int)P.V, 0.f,
+                  sid, skey, -1};
   const int words = (X.V + 31) / 32;
   for (int w = tid; w < words; w += NT) bm.word(w) = 0u;
   cbar();
@@ -966,25 +1333,68 @@ __device__ __noinline__ void exact_row(const KParams& P, const RowCfg& c, int ro
     const int64_t a = P.hrow[row], b = P.hrow[row + 1];
     X.hist_a = lower_bound_ids(P.hids, a, b, P.voff);
     X.hist_b = lower_bound_ids(P.hids, X.hist_a, b, P.voff + X.V);
+    const int64_t nh = X.hist_b - X.hist_a;
+    X.ns = nh <= XSTAGE ? (int)nh : -1;
     for (int64_t q = X.hist_a + tid; q < X.hist_b; q += NT) {
-      if (__ldg(P.hcnt + q) > 0) {
-        const int i = (int)(__ldg(P.hids + q) - P.voff);
-        atomicOr(&bm.word(i >> 5), 1u << (i & 31));
+      const int i = (int)(__ldg(P.hids + q) - P.voff);
+      const int cn = __ldg(P.hcnt + q);
+      if (cn > 0) atomicOr(&bm.word(i >> 5), 1u << (i & 31));
+      if (X.ns >= 0) {
+        sid[q - X.hist_a] = i;
+        skey[q - X.hist_a] =
+            cn > 0 ? okey(vf(penalize(Elem<TIn>::ld(X.rowp, i), cn, c), c)) : 0u;
       }
     }
   }
   cbar();
-  // maximum (and, for greedy rows, the first index of it)
-  unsigned long long best = ~0ull;
-  for (int i = tid; i < X.V; i += NT) {
-    const unsigned long long cc = comp(X.key_at(i), (int)(P.voff + i));
-    best = cc < best ? cc : best;
-  }
-  best = cta_min_u64(best, S);
-  X.mv = from_okey(comp_key(best));
-  if (c.greedy) {
+  const float NO_BOUND = __int_as_float(0x7fc00000);  // an open upper bound of row_pass
+  if (c.greedy) {  // the first index of the maximum (keys are the penalised logits themselves)
+    unsigned long long best = ~0ull;
+    row_pass(X, -INFINITY, NO_BOUND, [&](bool ok, uint32_t key, int i) {
+      if (!ok) return;
+      const unsigned long long cc = comp(key, (int)(P.voff + i));
+      best = cc < best ? cc : best;
+    });
+    best = cta_min_u64(best, S);
     if (tid == 0) write_state(P, row, 2, comp_id(best), 0.f, 0.f, 0u, 0);
     return;
+  }
+  // the largest processed value: vf is monotone, so the largest raw logit of the positions
+  // without penalty gives theirs with one division; penalised positions bring their keys. A
+  // NaN with the sign bit clear is the largest key of all (the row is then refused below).
+  {
+    using E = Elem<TIn>;
+    uint32_t kb = 0u;
+    float ymax = -INFINITY;
+    bool pnan = false;
+    auto one = [&](bool maybe_pen, float y, int i) {
+      if (maybe_pen && bm.bit(i)) {
+        kb = max(kb, X.pen_key(i));
+      } else {
+        ymax = fmaxf(ymax, y);
+        pnan = pnan || (__float_as_uint(y) - 0x7F800001u) < 0x007FFFFFu;
+      }
+    };
+    row_walk<TIn>(
+        X.rowp, X.V,
+        [&](uint4 q, int i0, bool vv) {
+          if (!vv) return;
+          if (c.pen && bits_any(bm, X.V, i0, E::A)) {
+#pragma unroll 1
+            for (int e = 0; e < E::A; ++e) {
+              one(true, E::at(q, 0), i0 + e);
+              shift_elem<TIn>(q);
+            }
+          } else {
+            ymax = fmaxf(ymax, E::vmax(q));
+            pnan = pnan || E::pos_nan(q);
+          }
+        },
+        [&](bool valid, float y, int i) {
+          if (valid) one(c.pen, y, i);
+        });
+    kb = pnan ? 0xFFC00000u : max(kb, okey(vf(ymax, c)));
+    X.mv = from_okey(cta_max_u32(kb, S));
   }
   if (!(X.mv > -INFINITY) || !(X.mv <= FLT_MAX)) {
     if (tid == 0) {
@@ -993,66 +1403,42 @@ __device__ __noinline__ void exact_row(const KParams& P, const RowCfg& c, int ro
     }
     return;
   }
-  // top-k threshold: radix select over the keys of the whole row (8-bit digits)
+  // top-k threshold: the key of the k-th element in canonical order (ties of it kept)
   uint32_t tk = 0;
   if (c.topk) {
-    uint32_t* hist = S.bin_cnt;
-    uint32_t prefix = 0;
-    int need = c.k;
-#pragma unroll 1
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      const uint32_t hmask = pass == 0 ? 0u : (0xFFFFFFFFu << (shift + 8));
-      hist[tid] = 0;
-      cbar();
-      for (int base = 0; base < X.V; base += NT) {
-        const int i = base + tid;
-        bool ok = i < X.V;
-        uint32_t k = 0;
-        if (ok) {
-          k = X.key_at(i);
-          ok = (k & hmask) == prefix;
-        }
-        warp_bin_add(ok, (k >> shift) & 255u, 0ull, hist, nullptr);
-      }
-      cbar();
-      const int d = 255 - tid;
-      const int cnt = (int)hist[d];
-      int tot;
-      const int above = cta_excl_scan_i(cnt, &tot, S);
-      if (above < need && above + cnt >= need) {
-        S.sc[SC_B] = d;
-        S.sc[SC_J] = need - above;
-      }
-      cbar();
-      prefix |= (uint32_t)S.sc[SC_B] << shift;
-      need = S.sc[SC_J];
-      cbar();
-    }
-    tk = prefix;
+    const Cut all = {0u, 1, 0u, 0, 0u};
+    const Found fk =
+        exact_search(X, all, (unsigned long long)c.k, -1.0, false, false, S, nullptr, nullptr);
+    tk = fk.n_w > 0 ? fk.w : 0u;
   }
   const Cut base = {tk, 1, 0u, 0, 0u};
-  // total mass of the kept-by-top-k set, fixed point
-  unsigned long long part = 0;
-  for (int i = tid; i < X.V; i += NT) {
-    const uint32_t key = X.key_at(i);
-    if (base.keep(key, i)) part += X.wfx(key);
-  }
-  const unsigned long long S_fx = cta_sum_u64(part, S);
   Cut fin = base;
-  unsigned long long s_kept = S_fx;
+  unsigned long long S_fx = 0, s_kept = 0;
   bool cut_set = false;
+  Level0 l0 = {false, -1, 0ull, 0u, 0ull, 0u};
+  bool have_l0 = false;  // l0.mo/co: this thread's first-level bin of the top-k kept set
   if (c.p < 1.f) {
-    const unsigned long long tgt = (unsigned long long)((double)c.p * (double)S_fx);
-    const Found f = exact_search(X, base, tgt, false, S);
+    // the total kept mass comes with the first level of the search
+    const Found f = exact_search(X, base, 0ull, (double)c.p, false, true, S, &S_fx, &l0);
+    have_l0 = true;
+    s_kept = S_fx;
     if (f.n_w > 0) {
-      const int id = exact_jth(X, base, f.w, f.j, S);
+      const int id = found_index(X, base, f, S);
       fin.kind = 0;
       fin.ck = f.w;
       fin.cid = id;
       s_kept = f.above + (unsigned long long)f.j * X.wfx(f.w);
       cut_set = true;
     }
+  } else {
+    unsigned long long part = 0;
+    float ylo_k, yn_k;
+    raw_range(c, tk, 0xFFFFFFFFu, &ylo_k, &yn_k);
+    row_pass_sparse(X, ylo_k, yn_k, [&](uint32_t key, int i) {
+      if (base.keep(key, i)) part += X.wfx(key);
+    });
+    S_fx = cta_sum_u64(part, S);
+    s_kept = S_fx;
   }
   if (c.minp > 0.f) {
     // min-p keeps a prefix by value; it binds when the top-p cut lies below its threshold
@@ -1060,13 +1446,14 @@ __device__ __noinline__ void exact_row(const KParams& P, const RowCfg& c, int ro
     if (binds) {
       unsigned long long pm = 0;
       uint32_t kmin = 0xFFFFFFFFu;
-      for (int i = tid; i < X.V; i += NT) {
-        const uint32_t key = X.key_at(i);
-        if (!base.keep(key, i)) continue;
-        if ((from_okey(key) - X.mv) * LOG2E < c.lm) continue;
+      float ylo_k, yn_k;
+      raw_range(c, tk, 0xFFFFFFFFu, &ylo_k, &yn_k);
+      row_pass_sparse(X, ylo_k, yn_k, [&](uint32_t key, int i) {
+        if (!base.keep(key, i)) return;
+        if ((from_okey(key) - X.mv) * LOG2E < c.lm) return;
         pm += X.wfx(key);
         kmin = min(kmin, key);
-      }
+      });
       const unsigned long long pms = cta_sum_u64(pm, S);
       const uint32_t km = ~cta_max_u32(~kmin, S);
       fin = base;
@@ -1075,9 +1462,27 @@ __device__ __noinline__ void exact_row(const KParams& P, const RowCfg& c, int ro
     }
   }
   const unsigned long long tgt = (unsigned long long)((double)c.u * (double)s_kept);
-  const Found fd = exact_search(X, fin, tgt, true, S);
-  int tok = -1;
-  if (fd.n_w > 0) tok = exact_jth(X, fin, fd.w, fd.j, S);
+  if (have_l0) {
+    // the draw's first step from the top-p search's mass-scale bins (thread t holds bin t):
+    // bins above the cut's bin are kept whole, the cut's bin keeps s_kept less the bins above
+    // it, lower bins nothing
+    const bool cut_k = fin.kind == 0 || fin.mk != 0u;
+    const int cbin = cut_k ? dbin(fin.kind == 0 ? fin.ck : fin.mk, X.mv) : -1;
+    const unsigned long long m_above = cta_sum_u64(cut_k && tid < cbin ? l0.mo : 0ull, S);
+    l0.in = true;
+    l0.cut_bin = cbin;
+    l0.m = l0.mo;
+    l0.c = l0.co;
+    if (cut_k && tid == cbin) {
+      l0.m = s_kept - m_above;
+      l0.c = 1u;
+    } else if (cut_k && tid > cbin) {
+      l0.m = 0ull;
+      l0.c = 0u;
+    }
+  }
+  const Found fd = exact_search(X, fin, tgt, -1.0, true, true, S, nullptr, have_l0 ? &l0 : nullptr);
+  const int tok = found_index(X, fin, fd, S);
   if (tid == 0) {
     if (tok < 0) status_or(P, VINFER_ST_INTERNAL);
     const int gtok = tok < 0 ? -1 : (int)(P.voff + tok);
@@ -1808,7 +2213,7 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
 }
 
 template <typename TIn>
-__global__ void __launch_bounds__(NT, 3) k_stream(const KParams P) {
+__global__ void __launch_bounds__(NT, 3) k_stream(const __grid_constant__ KParams P) {
   extern __shared__ __align__(128) unsigned char smraw[];
   Smem& S = *reinterpret_cast<Smem*>(smraw);
   // k_finish may be scheduled as soon as SMs free up; it waits for this grid's records itself
@@ -1832,7 +2237,7 @@ __global__ void __launch_bounds__(NT, 3) k_stream(const KParams P) {
 // ---------------------------------------------------------------------------------------------
 
 template <typename TIn>
-__global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
+__global__ void __launch_bounds__(NT, 3) k_finish(const __grid_constant__ KParams P) {
   using E = Elem<TIn>;
   extern __shared__ __align__(128) unsigned char smraw[];
   Smem& S = *reinterpret_cast<Smem*>(smraw);
@@ -2129,7 +2534,7 @@ __global__ void __launch_bounds__(NT, 2) k_finish(const KParams P) {
 // ---------------------------------------------------------------------------------------------
 // merge of gathered shard records: one CTA per row
 template <typename TIn>
-__global__ void __launch_bounds__(NT, 1) k_merge(const KParams P, const unsigned char* recs,
+__global__ void __launch_bounds__(NT, 1) k_merge(const __grid_constant__ KParams P, const unsigned char* recs,
                                               int world, int* unresolved) {
   extern __shared__ __align__(128) unsigned char smraw[];
   Smem& S = *reinterpret_cast<Smem*>(smraw);
@@ -2140,7 +2545,7 @@ __global__ void __launch_bounds__(NT, 1) k_merge(const KParams P, const unsigned
 
 // final probabilities [B, V] from the row states (parity checks only)
 template <typename TIn>
-__global__ void __launch_bounds__(256) k_probs(const KParams P) {
+__global__ void __launch_bounds__(256) k_probs(const __grid_constant__ KParams P) {
   const int row = blockIdx.y;
   const RowCfg c = load_row(P, row);
   const RowState st = P.rows[row];
