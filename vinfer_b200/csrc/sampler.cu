@@ -54,7 +54,7 @@ constexpr int CAND_BUF = 2048;          // candidates held for the run being pro
 constexpr int SCRATCH = 4096;           // 8-byte words of the scratch region (32 KiB)
 constexpr int CAND_CAP = 1024;          // entries of one record
 constexpr int KMAX = 192;               // largest top-k served by the candidate path
-constexpr int KC = 64;                  // candidates kept per run when top-k is off
+constexpr int KC = 32;                  // candidates kept per run when top-k is off (< TB)
 constexpr int MAX_NSEG = 64;
 constexpr int CTA_CAP = 1024;          // resident CTAs assumed when sizing workspaces
 constexpr int MERGE_CAP = 2048;         // merged entries (input in cand, sorted in scratch)
@@ -1693,6 +1693,7 @@ __device__ __forceinline__ int dele_push(Smem& S, unsigned long long d) {
 }
 
 constexpr int TB = 64;  // the list is tightened once per block of TB delegates
+static_assert(KC < TB, "rows without top-k tighten on the KC-th delegate of a block");
 
 // A list entry once its writer has stored it (the list starts filled with ~0); gives up after a
 // bounded number of polls and reports the entry as absent, which only weakens the bound.
