@@ -964,16 +964,21 @@ __device__ __forceinline__ void row_pass_sparse(const ExactRow<TIn>& X, float yl
   cl.T = X.c.T;
   cl.greedy = X.c.greedy;
   const bool open_hi = !(ynext == ynext);  // NaN: no upper bound
+  // penalised positions come from the staged list after the walk (no lookup per element)
+  const bool staged = pen && X.ns >= 0;
   auto elem = [&](bool maybe_pen, float y, int i) {
-    if (maybe_pen && bm.bit(i)) f(X.pen_key(i), i);
-    else if (!(y < ylo) && !(y >= ynext)) f(okey(vf(y, cl)), i);
+    if (maybe_pen && bm.bit(i)) {
+      if (!staged) f(X.pen_key(i), i);
+    } else if (!(y < ylo) && !(y >= ynext)) {
+      f(okey(vf(y, cl)), i);
+    }
   };
   row_walk<TIn>(
       X.rowp, V,
       [&](uint4 q, int i0, bool vv) {
         if (!vv) return;
         const bool mp = pen && bits_any(bm, V, i0, A);
-        if (!mp && (E::vmax(q) < ylo || !(open_hi || E::vmin(q) < ynext))) return;
+        if ((!mp || staged) && (E::vmax(q) < ylo || !(open_hi || E::vmin(q) < ynext))) return;
 #pragma unroll 1
         for (int e = 0; e < A; ++e) {
           elem(mp, E::at(q, 0), i0 + e);
@@ -983,6 +988,11 @@ __device__ __forceinline__ void row_pass_sparse(const ExactRow<TIn>& X, float yl
       [&](bool valid, float y, int i) {
         if (valid) elem(pen, y, i);
       });
+  if (staged)
+    for (int s = threadIdx.x; s < X.ns; s += NT) {
+      const int i = X.sid[s];
+      if (bm.bit(i)) f(X.skey[s], i);
+    }
 }
 
 // Radix bins of the exact search: element counts and fixed-point masses. 64-bit shared-memory
@@ -1186,7 +1196,7 @@ __device__ Found exact_search(const ExactRow<TIn>& X, const Cut& cut_in,
     if (klo == khi) break;  // one key: a tie group too large to collect
     // ---- one step: bins over [klo, khi]; thread t holds the bin at position t in descending
     // key order
-    const bool dstep = step == 0 && mass_w;
+    const bool dstep = step == 0;
     int sh = 0;
     uint32_t base = 0u;
     if (!dstep) {
@@ -1367,9 +1377,10 @@ __device__ __noinline__ void exact_row(const KParams& P, const RowCfg& c, int ro
     uint32_t kb = 0u;
     float ymax = -INFINITY;
     bool pnan = false;
+    const bool staged = c.pen && X.ns >= 0;
     auto one = [&](bool maybe_pen, float y, int i) {
       if (maybe_pen && bm.bit(i)) {
-        kb = max(kb, X.pen_key(i));
+        if (!staged) kb = max(kb, X.pen_key(i));
       } else {
         ymax = fmaxf(ymax, y);
         pnan = pnan || (__float_as_uint(y) - 0x7F800001u) < 0x007FFFFFu;
@@ -1393,7 +1404,11 @@ __device__ __noinline__ void exact_row(const KParams& P, const RowCfg& c, int ro
         [&](bool valid, float y, int i) {
           if (valid) one(c.pen, y, i);
         });
+    if (staged)
+      for (int s = tid; s < X.ns; s += NT)
+        if (bm.bit(sid[s])) kb = max(kb, skey[s]);
     kb = pnan ? 0xFFC00000u : max(kb, okey(vf(ymax, c)));
+    S.ext[tid] = ymax;  // this thread's largest raw logit without penalty (the top-k floor)
     X.mv = from_okey(cta_max_u32(kb, S));
   }
   if (!(X.mv > -INFINITY) || !(X.mv <= FLT_MAX)) {
@@ -1403,10 +1418,25 @@ __device__ __noinline__ void exact_row(const KParams& P, const RowCfg& c, int ro
     }
     return;
   }
-  // top-k threshold: the key of the k-th element in canonical order (ties of it kept)
+  // top-k threshold: the key of the k-th element in canonical order (ties of it kept). The
+  // k-th largest of the threads' largest raw logits (distinct positions) bounds it from below
+  // for k <= 256, so only the positions above that bound are searched.
   uint32_t tk = 0;
   if (c.topk) {
-    const Cut all = {0u, 1, 0u, 0, 0u};
+    uint32_t kfl = 0u;
+    if (c.k <= NT) {
+      const float mine = S.ext[tid];
+      int rank = 0;
+      for (int t = 0; t < NT; ++t) {
+        const float o = S.ext[t];
+        rank += (o > mine) || (o == mine && t < tid);
+      }
+      const unsigned long long cand = rank == c.k - 1 && mine > -INFINITY
+                                          ? (unsigned long long)okey(vf(mine, c))
+                                          : 0ull;
+      kfl = (uint32_t)~cta_min_u64(~cand, S);
+    }
+    const Cut all = {kfl, 1, 0u, 0, 0u};
     const Found fk =
         exact_search(X, all, (unsigned long long)c.k, -1.0, false, false, S, nullptr, nullptr);
     tk = fk.n_w > 0 ? fk.w : 0u;
