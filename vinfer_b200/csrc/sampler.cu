@@ -153,7 +153,7 @@ struct __align__(16) Smem {
 
 // scalar slots in Smem::sc / Smem::sf
 enum { SC_NC = 0, SC_NRET, SC_TKEY, SC_LAST, SC_B, SC_J, SC_X0, SC_X1, SC_NQ, SC_RFL, SC_NH,
-       SC_FB };
+       SC_FB, SC_LOCK, SC_NBEST };
 enum { SF_TH = 0, SF_SK = 2, SF_M };
 
 // ---------------------------------------------------------------------------------------------
@@ -1849,6 +1849,201 @@ __device__ __forceinline__ unsigned long long warp_merge32(unsigned long long a,
 // tokens cannot lift the bound; with j > 1 they are not checked, and should penalties push
 // the bound above the row's K-th largest processed value, the finishing kernel detects it and
 // takes the exact search, so it only ever costs time. Published with atomicMax.
+// ---- rows with 32 < K <= KMAX: their own instantiation of the streaming loop (the code below
+// stays out of the K <= 32 loop's registers)
+
+// The K-th largest of the 256 ordered keys Smem::ext holds (as floats), by one warp: a radix
+// select bit by bit, each lane counting its eight keys and the warp summing the counts.
+__device__ __forceinline__ uint32_t warp_kth_of_256(int K, Smem& S) {
+  const int lane = threadIdx.x & 31;
+  const volatile float* ext = S.ext;
+  uint32_t key[NCW];
+#pragma unroll
+  for (int o = 0; o < NCW; ++o) key[o] = okey(ext[o * 32 + lane]);
+  uint32_t prefix = 0u;
+  int need = K;
+#pragma unroll 1
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t mask = ~((1u << bit) - 1u), cand = prefix | (1u << bit);
+    int c = 0;
+#pragma unroll
+    for (int o = 0; o < NCW; ++o) c += (key[o] & mask) == cand;
+    c = (int)__reduce_add_sync(FULLMASK, (unsigned)c);
+    if (c >= need) prefix = cand;
+    else need -= c;
+  }
+  return prefix;
+}
+
+// Ascending sort of 64 keys held two per lane (a: element lane, b: element lane + 32), bitonic.
+__device__ __forceinline__ void warp_sort64(unsigned long long& a, unsigned long long& b) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j == 32) {  // pairs (lane, lane + 32), ascending (k = 64)
+        const unsigned long long lo = a < b ? a : b, hi = a < b ? b : a;
+        a = lo;
+        b = hi;
+      } else {
+        const unsigned long long pa = __shfl_xor_sync(FULLMASK, a, j);
+        const unsigned long long pb = __shfl_xor_sync(FULLMASK, b, j);
+        const bool low = (lane & j) == 0;  // the lower index of its pair
+        const bool upa = (lane & k) == 0, upb = ((lane + 32) & k) == 0;
+        a = (low == upa) ? (a < pa ? a : pa) : (a < pa ? pa : a);
+        b = (low == upb) ? (b < pb ? b : pb) : (b < pb ? pb : b);
+      }
+    }
+  }
+}
+
+// One block says little about a K-th largest with K > 32, so these rows keep the K best
+// unflagged delegates seen so far (sorted, canonical order; Smem::bin_mass is free while
+// streaming) and the warp that completes a block merges the block into them and raises the
+// threshold to their K-th. One warp merges at a time; a block that finds the list busy is left
+// out, which only leaves the bound looser (any K distinct elements bound the K-th largest).
+static_assert(KMAX + TB <= 256, "the best list and a sorted block fit Smem::bin_mass");
+__device__ __noinline__ void best_merge(const KParams& P, int b0, int K, float T, bool greedy,
+                                        bool pen, int vec_len, Smem& S) {
+  const int lane = threadIdx.x & 31;
+  int got = 0;
+  if (lane == 0) got = atomicCAS(&S.sc[SC_LOCK], 0, 1) == 0;
+  if (!__shfl_sync(FULLMASK, got, 0)) return;
+  __threadfence_block();
+  unsigned long long* best = S.bin_mass;        // [KMAX]
+  unsigned long long* blk = S.bin_mass + KMAX;  // [TB]
+  auto ent = [&](int i) {
+    unsigned long long v = list_entry(S, i);
+    if (pen && v != ~0ull) {
+      const RunHist h = hist_view(P, S);
+      if (hist_any(h, (int)((uint32_t)v & DL_ID), ((uint32_t)v & DL_ONE) ? 1 : vec_len)) v = ~0ull;
+    }
+    return v;
+  };
+  unsigned long long a = ent(b0 + lane), b = ent(b0 + 32 + lane);
+  warp_sort64(a, b);
+  blk[lane] = a;
+  blk[32 + lane] = b;
+  const int na = *reinterpret_cast<volatile int*>(&S.sc[SC_NBEST]);
+  const int nb = __popc(__ballot_sync(FULLMASK, a != ~0ull)) + __popc(__ballot_sync(FULLMASK, b != ~0ull));
+  __syncwarp();
+  // outputs o = lane + 32 t of the merge of best[0, na) and blk[0, nb): merge path
+  const int nout = min(K, na + nb);
+  unsigned long long out[(KMAX + 31) / 32];
+#pragma unroll
+  for (int t = 0; t < (KMAX + 31) / 32; ++t) {
+    const int o = lane + 32 * t;
+    out[t] = ~0ull;
+    if (o < nout) {
+      int lo = max(0, o - nb), hi = min(o, na);
+      while (lo < hi) {  // elements of best among the first o outputs
+        const int mid = (lo + hi) >> 1;
+        if (best[mid] < blk[o - 1 - mid]) lo = mid + 1; else hi = mid;
+      }
+      const int j = o - lo;
+      out[t] = (j >= nb || (lo < na && best[lo] < blk[j])) ? best[lo] : blk[j];
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int t = 0; t < (KMAX + 31) / 32; ++t) {
+    const int o = lane + 32 * t;
+    if (o < nout) best[o] = out[t];
+  }
+  unsigned long long kth = ~0ull;
+#pragma unroll
+  for (int t = 0; t < (KMAX + 31) / 32; ++t)
+    if (nout == K && t == ((K - 1) >> 5)) kth = __shfl_sync(FULLMASK, out[t], (K - 1) & 31);
+  __syncwarp();
+  if (lane == 0) *reinterpret_cast<volatile int*>(&S.sc[SC_NBEST]) = nout;
+  if (kth != ~0ull) {
+    RowCfg c{};
+    c.T = T;
+    c.greedy = greedy;
+    const float y = ylo_for(vf(dele_max(kth), c), c);
+    if (lane == 0) atomicMax(&S.ylo_key, okey(y));
+  }
+  __threadfence_block();
+  __syncwarp();
+  if (lane == 0) atomicExch(&S.sc[SC_LOCK], 0);
+}
+
+// First bounds of a large-K row, from the first segment. At once, per warp: the q-th largest
+// of its lanes' j-th largest vector maxima (j = ceil(K / 32), q = ceil(K / j): q lanes with j
+// vectors each reach it). Then, by the last warp to publish: the K-th largest of the 256 lanes'
+// largest vector maxima (a lane's is left out when that vector holds a history id), which is
+// much tighter. Both are bounds on the row's K-th largest.
+template <typename TIn>
+__device__ __forceinline__ void wide_first_bound(const KParams& P, const SegLoad<TIn>& L,
+                                                 const float* vm, int K, float T, bool greedy,
+                                                 bool pen, Smem& S) {
+  constexpr int A = Elem<TIn>::A;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int j = (K + 31) / 32;
+  float v[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) v[u] = vm[u];
+  float l1 = -INFINITY, lv = -INFINITY;
+  int u1 = -1;
+  for (int r = 0; r < j; ++r) {  // the lane's r-th largest vector maximum
+    float m = -INFINITY;
+    int mu = -1;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (v[u] > m) {
+        m = v[u];
+        mu = u;
+      }
+    lv = m;
+    if (r == 0) {
+      l1 = m;
+      u1 = mu;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (u == mu) v[u] = -INFINITY;
+  }
+  float x = lv;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {  // descending bitonic sort of the 32 lane values
+#pragma unroll
+    for (int jj = k >> 1; jj > 0; jj >>= 1) {
+      const float o = __shfl_xor_sync(FULLMASK, x, jj);
+      const bool lower = (lane & jj) == 0, up = (lane & k) == 0;
+      x = (lower == up) ? fmaxf(x, o) : fminf(x, o);
+    }
+  }
+  const float tw = __shfl_sync(FULLMASK, x, (K + j - 1) / j - 1);
+  if (tw > -INFINITY) {
+    RowCfg c{};
+    c.T = T;
+    c.greedy = greedy;
+    const float y = ylo_for(vf(tw, c), c);
+    if (lane == 0) atomicMax(&S.ylo_key, okey(y));
+  }
+  if (pen && u1 >= 0 &&
+      hist_any(hist_view(P, S), (int)(L.gid0 + (int64_t)(tid + NT * u1) * A), A))
+    l1 = -INFINITY;
+  S.ext[tid] = l1;
+  __threadfence_block();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = atomicAdd(&S.sc[SC_FB], 1) == NCW - 1;
+  if (__shfl_sync(FULLMASK, last, 0)) {
+    __threadfence_block();
+    const float tc = from_okey(warp_kth_of_256(K, S));
+    if (tc > -INFINITY) {
+      RowCfg c{};
+      c.T = T;
+      c.greedy = greedy;
+      const float y = ylo_for(vf(tc, c), c);
+      if (lane == 0) atomicMax(&S.ylo_key, okey(y));
+    }
+  }
+  __syncwarp();
+}
+
 template <typename TIn>
 __device__ __forceinline__ void warp_first_bound(const KParams& P, const SegLoad<TIn>& L,
                                                  const float* vm, int K, float T, bool greedy,
@@ -1947,7 +2142,7 @@ enum { MODE_GREEDY = 0, MODE_CANDS = 1, MODE_CANDS_SUM = 2 };
 // The streaming loop of one run, specialised per kind of row so each variant keeps only its
 // own state in registers: MODE 0 greedy (first index of the maximum), 1 candidates, 2
 // candidates plus the online softmax sum of rows without top-k.
-template <typename TIn, int MODE>
+template <typename TIn, int MODE, bool BIGK = false>
 __device__ __forceinline__ void stream_run(const KParams& P, Smem& S, int row, int seg_a,
                                            int seg_b, int K, float T, float c2, bool greedy,
                                            bool pen, SegLoad<TIn>& sa, float& m_t, float& s_t,
@@ -1998,7 +2193,10 @@ __device__ __forceinline__ void stream_run(const KParams& P, Smem& S, int row, i
       }
       return;
     }
-    if (seg == seg_a) warp_first_bound<TIn>(P, L, vm, K, T, greedy, pen, S);
+    if (seg == seg_a) {
+      if (BIGK) wide_first_bound<TIn>(P, L, vm, K, T, greedy, pen, S);
+      else warp_first_bound<TIn>(P, L, vm, K, T, greedy, pen, S);
+    }
     // the CTA's threshold as it stands: warps raise it as they go
     const float ylo = from_okey(*reinterpret_cast<volatile uint32_t*>(&S.ylo_key));
     int trig = -1;  // a block of the list this thread completed
@@ -2018,7 +2216,9 @@ __device__ __forceinline__ void stream_run(const KParams& P, Smem& S, int row, i
     while (tb) {  // rare: this warp completed a block of delegates
       const int src = __ffs(tb) - 1;
       tb &= tb - 1;
-      block_tighten(P, __shfl_sync(FULLMASK, trig, src), K, T, greedy, pen, A, S);
+      const int b0 = __shfl_sync(FULLMASK, trig, src);
+      if (BIGK) best_merge(P, b0, K, T, greedy, pen, A, S);
+      else block_tighten(P, b0, K, T, greedy, pen, A, S);
     }
   };
   // one segment in flight per CTA: the other resident CTAs of the SM keep loads outstanding
@@ -2093,6 +2293,8 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
     S.sc[SC_NRET] = 0;
     S.ylo_key = okey(-INFINITY);
     S.dkth = ~0ull;
+    S.sc[SC_LOCK] = 0;
+    S.sc[SC_NBEST] = 0;
   }
   for (int i = tid; i < CAND_BUF; i += NT) S.cand[i] = ~0ull;
   float m_t = -FLT_MAX, s_t = 0.f;
@@ -2116,6 +2318,9 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
   else if (need_sum)
     stream_run<TIn, MODE_CANDS_SUM>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first,
                                     m_t, s_t, gbest);
+  else if (K > 32)
+    stream_run<TIn, MODE_CANDS, true>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first, m_t,
+                                      s_t, gbest);
   else
     stream_run<TIn, MODE_CANDS>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first, m_t, s_t,
                                 gbest);
