@@ -6,27 +6,20 @@
 // repetition / presence / frequency penalties, min-p and an inverse-CDF draw from a caller
 // uniform. Tokens are ordered canonically: descending processed logit, ties by ascending id.
 //
-// Execution (one launch of k_sample per batch):
-//   * Work items are (row, segment) pairs; a segment is <= 32 KiB of one row's logits. The grid
-//     is persistent (two CTAs per SM): CTA b takes items b, b + grid, b + 2 grid, ...
-//   * Each CTA has two producer warps and eight consumer warps. Producer warp p owns shared
-//     stage p: it reads the row's parameters, finds the segment's slice of the row's sorted
-//     history (warp-cooperative search), loads those entries and the unaligned edges, then
-//     copies the 16-byte-aligned interior of the segment HBM -> shared memory with one TMA bulk
-//     copy per 16 KiB on an mbarrier. Metadata for the next item is fetched before the stage
-//     is free, so the consumers find each stage full when they get to it.
-//   * Consumers take penalised tokens out of the staged copy (exact float32 side values), make
-//     one pass computing per-thread maxima (plus an online softmax sum when top-k is off),
-//     extract the K largest per-thread maxima per warp (K distinct elements, so their K-th
-//     largest bounds the segment's K-th largest value from below), collect every element at or
-//     above that bound, rank the candidates by counting and write the top K with all ties,
-//     sorted, as the segment's record.
-//   * The CTA that completes a row's last record (acq_rel atomic counter, result consumed one
-//     item later so its latency is hidden) merges the row: sorted records -> merged by rank,
-//     top-k, top-p and min-p cuts by prefix sums, and the draw. A row whose cut or draw lies
-//     below what the records hold completely, or whose candidates overflowed, is finished by an
-//     exact multi-pass search over the row (radix histograms of mass in 2^-44 fixed point, ties
-//     resolved in id order) in the same CTA.
+// Execution (two launches per batch; sharded mode adds an all-gather and k_merge):
+//   * k_stream streams every row once. A row is cut into runs of whole segments (64 KiB: one
+//     round of 16-byte loads of the CTA, held in registers); with fewer rows than resident CTAs
+//     each run is one CTA's. Per vector only its maximum is compared with the CTA's threshold
+//     (a shared word raised as the run goes: the K-th largest of K distinct history-free
+//     vector maxima, from the first segment, then from blocks of noted "delegate" vectors).
+//     At the end of the run the delegates at or above the final threshold are read again and
+//     expanded into exact candidates; top-k rows add their penalised tokens with exact values.
+//     The run's record is counted on a per-row counter (release).
+//   * k_finish is launched as a programmatic dependent of k_stream: one CTA per row starts as
+//     SMs free up, waits (bounded) for its row's runs, selects the K largest candidates, checks
+//     that the K-th reaches every run's threshold, applies top-p / min-p by prefix sums and
+//     draws. Rows the candidates cannot decide take an exact search over the row (key-interval
+//     refinement with count and fixed-point mass histograms, 2^-44 units, ties in id order).
 //
 // All reductions run in a fixed order, so results are deterministic run to run.
 
@@ -48,8 +41,8 @@ namespace {
 // ---------------------------------------------------------------------------------------------
 constexpr int NCW = 8;                  // warps per CTA
 constexpr int NT = NCW * 32;            // threads per CTA
-constexpr int U = 8;                    // 16-byte vectors a thread loads per segment
-constexpr int SEG_BYTES = NT * U * 16;  // 32 KiB: one round of loads of the CTA
+constexpr int U = 16;                   // 16-byte vectors a thread loads per segment
+constexpr int SEG_BYTES = NT * U * 16;  // 64 KiB: one round of loads of the CTA
 constexpr int CAND_BUF = 2048;          // candidates held for the run being processed
 constexpr int SCRATCH = 4096;           // 8-byte words of the scratch region (32 KiB)
 constexpr int CAND_CAP = 1024;          // entries of one record
@@ -2221,8 +2214,8 @@ __device__ __forceinline__ void stream_run(const KParams& P, Smem& S, int row, i
       else block_tighten(P, b0, K, T, greedy, pen, A, S);
     }
   };
-  // one segment in flight per CTA: the other resident CTAs of the SM keep loads outstanding
-  // while this one processes (a second register buffer would not fit three CTAs per SM)
+  // one segment in flight per CTA (64 KiB): the other resident CTA of the SM keeps its loads
+  // outstanding while this one processes
   for (int seg = seg_a; seg <= seg_b; ++seg) {
     if (seg > seg_a) load_segment<TIn>(P, rowp, seg, sa);  // the first was issued by run()
     process(sa, seg);
@@ -2449,7 +2442,7 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
 }
 
 template <typename TIn>
-__global__ void __launch_bounds__(NT, 3) k_stream(const __grid_constant__ KParams P) {
+__global__ void __launch_bounds__(NT, 2) k_stream(const __grid_constant__ KParams P) {
   extern __shared__ __align__(128) unsigned char smraw[];
   Smem& S = *reinterpret_cast<Smem*>(smraw);
   // k_finish may be scheduled as soon as SMs free up; it waits for this grid's records itself
