@@ -844,7 +844,7 @@ __device__ __forceinline__ bool bits_any(const RowBits& bm, int V, int i0, int n
 template <typename TIn>
 __device__ __forceinline__ void shift_elem(uint4& q) {
   constexpr int SB = 128 / Elem<TIn>::A;  // bits per element
-  if (SB == 32) {
+  if constexpr (SB == 32) {
     q.x = q.y;
     q.y = q.z;
     q.z = q.w;
