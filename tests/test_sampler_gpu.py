@@ -288,3 +288,27 @@ def test_penalised_rows_without_top_k(backend):
     ids, probs = run_b200(backend, w)
     rep = compare(w, ids, probs)
     assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+@pytest.mark.parametrize("k", [40, 100, 150])
+@pytest.mark.parametrize("batch,V", [(3, 151_936), (320, 20_000)])
+def test_large_top_k_with_penalised_top_tokens(backend, k, batch, V):
+    # rows with 32 < K <= 192 stream in a loop of their own (a running list of the K best
+    # delegates); penalising the largest logits checks that delegates holding history ids never
+    # lift the threshold. Three rows are cut into many runs; 320 rows share the CTAs.
+    g = torch.Generator().manual_seed(1000 * k + batch)
+    kinds = [dict(temperature=0.7, top_k=k, top_p=0.8, repetition_penalty=1.1,
+                  presence_penalty=0.5, frequency_penalty=0.3),
+             dict(temperature=1.0, top_k=k, repetition_penalty=1.5),
+             dict(temperature=0.6, top_k=k, min_p=0.01, frequency_penalty=0.8)]
+    params = [kinds[r % len(kinds)] for r in range(batch)]
+    x = (torch.randn(batch, V, generator=g) * 2.0).to(torch.bfloat16)
+    rng = np.random.default_rng(k + batch)
+    rows = []
+    for r in range(batch):
+        top = torch.topk(x[r].float(), 2 * k).indices.numpy()
+        rows.append(np.concatenate([top, rng.integers(0, V, 300)]))
+    w = _workload(x, params, hist=_hist_csr(rows))
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    assert not rep.failures, (str(rep), rep.failures[:5])
