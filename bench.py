@@ -315,6 +315,123 @@ def bench_single(args) -> dict:
 
 
 # ----------------------------------------------------------------------------------------------
+# single GPU, --workload config4: configuration 4 unsharded (the strong-scaling reference for the
+# vocab-sharded runs; not the default line)
+# ----------------------------------------------------------------------------------------------
+def bench_single_config4(args) -> dict:
+    from vinfer_b200 import SAMPLER, BackendContext  # noqa: PLC0415
+    from vinfer_b200.workloads import config4_shard  # noqa: PLC0415
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, V = 1024, 248_320
+    backend = SAMPLER.resolve("b200", BackendContext(dev, torch.bfloat16))
+    x, params, u = config4_shard(0, 1, dev, B, V)
+    nbytes = x.numel() * x.element_size()
+    nbuf = max(2, int(np.ceil(2 * L2_BYTES / nbytes)) + 1)
+    bufs = [x] + [x.clone() for _ in range(nbuf - 1)]
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i: int) -> None:
+        backend.sample_batch(bufs[i % nbuf], params, u, None, out=out)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    backend.check()
+    torch.cuda._sleep(20_000_000)
+    pairs = []
+    for i in range(16):
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record(stream)
+        step(i)
+        e_.record(stream)
+        pairs.append((s_, e_))
+    torch.cuda.synchronize()
+    kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in pairs)
+
+    K = args.steps
+    clocks = Clocks(0)
+    clocks.start()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(K):
+        step(i)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    total_ms = t0.elapsed_time(t1)
+    clk = clocks.stop()
+    backend.check()
+
+    # end to end: the logits, the row parameters and the uniforms from pinned host memory
+    host_x = x.cpu().pin_memory()
+    host_p = {k: getattr(params, k).cpu().pin_memory() for k in
+              ("temperature", "top_k", "top_p", "min_p", "repetition_penalty",
+               "presence_penalty", "frequency_penalty")}
+    host_u = u.cpu().pin_memory()
+    host_ids = torch.empty(B, dtype=torch.int32).pin_memory()
+    d_x, d_u = torch.empty_like(x), torch.empty_like(u)
+    h2d = (nbytes + host_u.numel() * 4 + sum(t.numel() * t.element_size()
+                                              for t in host_p.values()))
+
+    def e2e_step() -> None:
+        d_x.copy_(host_x, non_blocking=True)
+        for k, t in host_p.items():
+            getattr(params, k).copy_(t, non_blocking=True)
+        d_u.copy_(host_u, non_blocking=True)
+        ids = backend.sample_batch(d_x, params, d_u, None, out=out)
+        host_ids.copy_(ids, non_blocking=True)
+
+    e2e_steps = max(3, min(K, 20))
+    e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    backend.check()
+
+    peak, kind = measured_peak()
+    algo = B * V * 2 + 36 * B
+    achieved = algo / (kernel_ms * 1e-3) / 1e9
+    return {
+        "metric": METRIC,
+        "value": B * K / (total_ms * 1e-3),
+        "unit": "rows/s",
+        "n_gpus": 1,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": total_ms / K,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded on the device, configuration 4 distribution)",
+        "config": {"workload": "config4 unsharded: batch 1024 x vocab 248320 bf16 N(0,3) + 4 "
+                               "spikes on one GPU, temp 1, top-k 50, top-p 0.9",
+                   "batch": B, "vocab": V,
+                   "l2": f"{nbuf} rotating logits buffers "
+                         f"({nbuf * nbytes / 2**20:.0f} MiB > 2x L2)",
+                   "parallelism": "single GPU"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": f"{kind} (copy bandwidth)",
+                     "traffic": None, "algorithmic_bytes": algo,
+                     "kernel": "k_stream<bf16> + k_finish<bf16> (one sample_batch)",
+                     "kernel_ms": kernel_ms},
+        "clocks": clk,
+        "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "rows/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": B * 4, "steps": e2e_steps},
+        "gpu_launches": 2 * K,  # k_stream and k_finish per step
+        "cpu_baseline": None,
+    }
+
+
+# ----------------------------------------------------------------------------------------------
 # N > 1: configuration 4, vocab-sharded (one process per GPU, NCCL)
 # ----------------------------------------------------------------------------------------------
 def bench_sharded(args) -> dict | None:
@@ -514,6 +631,9 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["default", "config4"], default="default",
+                    help="one GPU only: config4 times configuration 4 unsharded (the reference "
+                         "for the vocab-sharded runs); the default line is configuration 3")
     args = ap.parse_args()
     rank, world, local = dist_env()
     if args.impl == "reference":
@@ -525,6 +645,8 @@ def main() -> None:
     elif args.gpus > 1:
         raise SystemExit("--gpus N > 1 runs one process per GPU: launch bench.py under "
                          "torch.distributed.run with --nproc-per-node N")
+    elif args.workload == "config4":
+        line = bench_single_config4(args)
     else:
         line = bench_single(args)
     if line is not None and rank == 0:
