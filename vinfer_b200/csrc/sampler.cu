@@ -2937,7 +2937,7 @@ int kernel_info(const void* kern, int slot, int threads, int* ctas) {
   return VINFER_OK;
 }
 
-// resident CTAs of k_sample on the current device (at most CTA_CAP)
+// resident CTAs of k_stream on the current device (at most CTA_CAP)
 int sample_ctas(int dtype, int* ctas) {
   const void* kern = dtype == VINFER_DTYPE_BF16 ? (const void*)k_stream<__nv_bfloat16>
                                                 : (const void*)k_stream<float>;
