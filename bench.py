@@ -171,6 +171,13 @@ def bench_single(args) -> dict:
     torch.cuda.set_device(dev)
     w = make(3)
     B, V = w.batch, w.vocab
+    topp = args.workload == "topp"
+    if topp:  # configuration 3's logits, top-p only: the rows the candidates cannot decide
+        w.top_k = np.zeros(B, np.int32)
+        w.top_p = np.full(B, 0.9, np.float32)
+        w.repetition_penalty = np.ones(B, np.float32)
+        w.presence_penalty = np.zeros(B, np.float32)
+        w.frequency_penalty = np.zeros(B, np.float32)
     backend = SAMPLER.resolve("b200", BackendContext(dev, torch.bfloat16))
     nbuf = max(4, int(np.ceil(2 * L2_BYTES / (w.logits.numel() * 2))) + 1)
     base = w.logits.to(dev)
@@ -277,10 +284,11 @@ def bench_single(args) -> dict:
         raise RuntimeError("e2e ids differ from the device result")
 
     peak, peak_kind = measured_peak()
-    algo = w.algorithmic_bytes()
+    algo = w.algorithmic_bytes() if not topp else B * V * 2 + 36 * B  # no penalties: no history
     achieved = algo / (kernel_ms * 1e-3) / 1e9
-    traffic = ncu_traffic("config3")
-    cpu = None if args.no_cpu_baseline else cpu_reference_rows_per_s(w, args.cpu_seconds)
+    traffic = ncu_traffic("config3") if not topp else None
+    cpu = (None if args.no_cpu_baseline or topp
+           else cpu_reference_rows_per_s(w, args.cpu_seconds))
     ms_step = total_ms / K
     return {
         "metric": METRIC,
@@ -295,8 +303,10 @@ def bench_single(args) -> dict:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded, configuration 3)",
-        "config": {"workload": CONFIG3_WORKLOAD,
-                   "batch": B, "vocab": V, "hist_nnz": w.hist_nnz,
+        "config": {"workload": CONFIG3_WORKLOAD if not topp else
+                   ("config3 logits, top-p only: batch 256 x vocab 151936 bf16, temp 0.7, "
+                    "top-k 0, top-p 0.9, no penalties (rows that need the exact search)"),
+                   "batch": B, "vocab": V, "hist_nnz": w.hist_nnz if not topp else 0,
                    "l2": f"{nbuf} rotating logits buffers "
                          f"({nbuf * w.logits.numel() * 2 / 2**20:.0f} MiB > 2x L2)",
                    "parallelism": "single GPU", "graph_steps": G},
@@ -631,9 +641,10 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["default", "config4"], default="default",
+    ap.add_argument("--workload", choices=["default", "config4", "topp"], default="default",
                     help="one GPU only: config4 times configuration 4 unsharded (the reference "
-                         "for the vocab-sharded runs); the default line is configuration 3")
+                         "for the vocab-sharded runs); topp times configuration 3's logits with "
+                         "top-p only (the exact search); the default line is configuration 3")
     args = ap.parse_args()
     rank, world, local = dist_env()
     if args.impl == "reference":
