@@ -159,8 +159,11 @@ class ShardedSampler:
         dist.all_gather_into_tensor(buf["gathered"], buf["local"], group=self.group)
         self.kernels.merge(logits, params, uniforms, history, lo, vocab_total, self.record_cap,
                            buf["gathered"], self.world, out, buf["unresolved"], probs_out)
-        # identical on every rank: all ranks take the fallback for the same rows
-        n = int(torch.count_nonzero(buf["unresolved"]))
+        # identical on every rank: all ranks take the fallback for the same rows. One boolean
+        # read per step (the count only when some row is unresolved, which is rare).
+        n = 0
+        if bool(buf["unresolved"].any()):
+            n = int(torch.count_nonzero(buf["unresolved"]))
         self.last_unresolved = n
         if n:
             self._resolve(logits, params, uniforms, history, vocab_total, out, probs_out,
