@@ -19,6 +19,8 @@ from oracle.sampler_oracle import RowResult, process_row
 from vinfer_b200.sampling import RowParams, TokenHistogram
 from vinfer_b200.workloads import Workload
 
+import warnings
+
 PROB_RTOL = 1e-5  # north-star tolerance on processed probabilities (relative, float32)
 TINY = 1e-30  # probabilities this small are compared for presence only
 
@@ -101,3 +103,12 @@ def compare(w: Workload, ids: np.ndarray, probs: np.ndarray | None,
             if rel.size and rel.max() > PROB_RTOL:
                 rep.failures.append((r, "probs", float(rel.max()), PROB_RTOL))
     return rep
+
+
+class ParityReport(UserWarning):
+    """A parity comparison's counts (rows, boundary rows, failures), reported in pytest's
+    warnings summary so every run's log records them."""
+
+
+def report(name: str, rep: Report) -> None:
+    warnings.warn(f"parity {name}: {rep}", ParityReport, stacklevel=2)

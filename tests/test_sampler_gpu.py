@@ -12,7 +12,9 @@ import numpy as np
 import pytest
 import torch
 
-from tests.helpers import compare, oracle_row, run_b200, to_device
+import ctypes as C
+
+from tests.helpers import compare, oracle_row, report, run_b200, to_device
 from vinfer_b200 import SAMPLER, BackendContext, SamplingParams, position_uniform
 from vinfer_b200 import _lib
 from vinfer_b200.sampling import RowParams
@@ -101,7 +103,7 @@ def test_benchmark_configs_match_the_oracle(backend, config, batch):
     w = make(config, batch=batch)
     ids, probs = run_b200(backend, w)
     rep = compare(w, ids, probs)
-    print(f"config {config}: {rep}")
+    report(f"config {config} (batch {w.batch})", rep)
     assert not rep.failures, (str(rep), rep.failures[:5])
 
 
@@ -109,7 +111,7 @@ def test_config5_every_row_class(backend):
     w = make(5, batch=32)  # eight rows of each class: flat, dominant, 1000-way tie, normal
     ids, probs = run_b200(backend, w)
     rep = compare(w, ids, probs)
-    print(f"config 5 classes: {rep}")
+    report("config 5 row classes (batch 32)", rep)
     assert not rep.failures, (str(rep), rep.failures[:5])
 
 
@@ -174,8 +176,52 @@ def test_full_batch_config3_is_deterministic_and_valid(backend):
     backend.check()
     np.testing.assert_array_equal(a, b)
     assert ((a >= 0) & (a < w.vocab)).all()
-    rep = compare(w, a, None, rows=list(range(0, 256, 32)))
+    rep = compare(w, a, None)  # every one of the 256 rows
+    report("config 3 ids, repeated call (batch 256)", rep)
     assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+@pytest.mark.parametrize("config", [2, 3, 5])
+def test_full_batch_configs_match_the_oracle(backend, config):
+    # the benchmark configurations at their full batch (64 / 256 / 512 rows): every row's id
+    # and every row's final probabilities against the oracle
+    w = make(config)
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    report(f"config {config} full batch ({w.batch} rows)", rep)
+    assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+def test_config4_unsharded_at_full_vocabulary(backend):
+    # configuration 4's rows (vocab 248,320, top-k 50, top-p 0.9) through vinfer_sample on one
+    # GPU: the single-GPU reference the sharded runs are compared with
+    w = make(4, batch=128)
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    report("config 4 unsharded (batch 128, vocab 248320)", rep)
+    assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+def test_one_workspace_serves_calls_of_different_shapes(backend):
+    # A workspace sized for the larger shape, used by 8 rows and then 24 rows (and 8 again):
+    # the per-row arrival counters sit in a header whose place does not depend on the shape,
+    # so no call finds another's records over its counters.
+    lib = backend.lib
+    small, large = make(3, batch=8), make(3, batch=24, seed=9)
+    nbytes = lib.vinfer_sampler_workspace_bytes(24, small.vocab, _lib.DTYPE_BF16)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=backend.device)
+    _lib.check(lib.vinfer_sampler_workspace_init(ws.data_ptr(), nbytes, backend._stream()),
+               "workspace init")
+    for w in (small, large, small, large):
+        lg, params, u, hist = to_device(w, backend.device)
+        out = torch.full((w.batch,), -7, dtype=torch.int32, device=backend.device)
+        a = backend.args(lg, params, u, hist, out, None)
+        _lib.check(lib.vinfer_sample(C.byref(a), ws.data_ptr(), nbytes, backend._stream()),
+                   "vinfer_sample")
+        torch.cuda.synchronize()
+        backend.check()
+        rep = compare(w, out.cpu().numpy(), None)
+        assert not rep.failures, (w.batch, str(rep), rep.failures[:5])
 
 
 def test_single_row_api_uses_the_position_uniform(backend):

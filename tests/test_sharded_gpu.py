@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from tests.helpers import compare, to_device
+from tests.helpers import compare, report, to_device
 from vinfer_b200 import SAMPLER, BackendContext
 from vinfer_b200.sharded import B200ShardKernels, select_rows, shard_range
 from vinfer_b200.workloads import make
@@ -83,7 +83,8 @@ def test_sharded_kernels_match_the_oracle(backend, config, batch, world):
     w = make(config, batch=batch)
     ids, probs, n_unres = emulate(backend, w, world)
     rep = compare(w, ids, probs)
-    print(f"config {config} over {world} shards: {rep}, {n_unres} rows via the full-row path")
+    report(f"config {config} over {world} shards (batch {batch}), {n_unres} rows via the "
+           "full-row path", rep)
     assert not rep.failures, (str(rep), rep.failures[:5])
 
 
