@@ -60,6 +60,28 @@ def _same(ref, got):
 
 
 @pytest.mark.gpu
+def test_static_call_allocates_no_device_memory():
+    # After a first call (which may load the library's device code and look up the scratch
+    # array's address), a call of another shape with its inputs and outputs already on the
+    # device must leave the device's free memory exactly as it was.
+    backend = SAMPLER.resolve("b200", BackendContext(torch.device("cuda", 0), torch.bfloat16))
+    _static_call(backend, make(3, batch=4), probs=False)
+    w = make(3, batch=40, seed=5)
+    lg, params, u, hist = to_device(w, backend.device)
+    out = torch.full((w.batch,), -7, dtype=torch.int32, device=backend.device)
+    a = backend.args(lg, params, u, hist, out, None)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    rc = backend.lib.vinfer_sample_static(C.byref(a), backend._stream())
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    _lib.check(rc, "vinfer_sample_static")
+    backend.check()
+    assert free1 == free0
+    assert ((out.cpu().numpy() >= 0) & (out.cpu().numpy() < w.vocab)).all()
+
+
+@pytest.mark.gpu
 def test_static_scratch_matches_the_workspace_entry_point():
     backend = SAMPLER.resolve("b200", BackendContext(torch.device("cuda", 0), torch.bfloat16))
     # two shapes in a row: rows split across many CTAs (per-row counters and run records in
@@ -73,12 +95,18 @@ def test_static_scratch_matches_the_workspace_entry_point():
 def test_shapes_beyond_the_static_scratch_are_refused():
     build()
     lib = _lib.load()
-    # the largest float32 vocabulary needs the most scratch per row; at least 63 rows fit
+    # any batch of up to 15,405 rows fits at any vocabulary; find the first that does not
     def ws(rows):
         return lib.vinfer_sampler_workspace_bytes(rows, _lib.MAX_VOCAB, _lib.DTYPE_F32)
-    too_big = 63
-    while ws(too_big) <= _lib.STATIC_SCRATCH_BYTES:
-        too_big += 1
+    lo, hi = 1, _lib.MAX_BATCH
+    while lo < hi:
+        mid = (lo + hi + 1) // 2
+        if ws(mid) <= _lib.STATIC_SCRATCH_BYTES:
+            lo = mid
+        else:
+            hi = mid - 1
+    assert lo >= 15405
+    too_big = lo + 1
     assert ws(too_big - 1) <= _lib.STATIC_SCRATCH_BYTES < ws(too_big)
     a = _lib.SampleArgs()
     a.logits = 256

@@ -3,7 +3,7 @@
 // finishing arithmetic and the exact search).
 //
 // One persistent CTA per SM, ten warps, each with one job and no CTA-wide barrier while
-// streaming. The batch is a row-major list of tiles (8 KiB of one row each); CTA b streams the
+// streaming. The batch is a row-major list of tiles (6 KiB of one row each); CTA b streams the
 // contiguous tiles [b * ntt / G, (b + 1) * ntt / G), so every CTA moves the same bytes. A CTA's
 // range meets a few rows; its piece of one row is a "part".
 //
@@ -11,7 +11,7 @@
 //     (one of two, alternating): the row's parameters, the part's history entries copied into
 //     shared memory by bulk copies, and the first entry of each tile in them. Then it copies the
 //     tiles into a 16-stage shared-memory ring with cp.async.bulk (TMA, no multicast), each
-//     stage's mbarrier counting the bytes. Up to 128 KiB per SM are in flight, about 2.7 us of
+//     stage's mbarrier counting the bytes. Up to 96 KiB per SM are in flight, about 2 us of
 //     the SM's share of HBM bandwidth.
 //   * Warps 0-7, the consumers: tile i of the range goes to warp i % 8 (stage i % 16, so each
 //     warp has one tile landing while it works on another). Per tile the warp first handles the
@@ -33,11 +33,13 @@
 
 constexpr int FW = 8;                          // consumer warps
 constexpr int FPROD = FW;                      // the producer warp
-constexpr int FFIN = FW + 1;                   // the finisher warps: FFIN (even parts) and
-constexpr int FNFIN = 2;                       //   FFIN + 1 (odd parts)
-constexpr int FNT = (FW + 1 + FNFIN) * 32;
+constexpr int FFIN = FW + 1;                   // the finisher warps: part p goes to
+constexpr int FNFIN = 2;                       //   FFIN + p % FNFIN
+constexpr int FPREP = FFIN + FNFIN;            // the warp that prepares the parts' slots
+constexpr int FNT = (FPREP + 1) * 32;
+constexpr int FNSLOT = 3;                      // parts in flight (prepared, streamed, finished)
 constexpr int FSTAGES = 16;                    // tiles in flight per CTA
-constexpr int FTILE = 8192;                    // bytes of one tile (one stage)
+constexpr int FTILE = 6144;                    // bytes of one tile (one stage)
 constexpr int FVEC = FTILE / 16;               // 16-byte vectors of a tile
 constexpr int FVPL = FVEC / 32;                // ... per lane of its warp
 constexpr int FHCAP = 2048;                    // history entries of a part staged in shared memory
@@ -47,11 +49,15 @@ constexpr int FSUMK = 64;                      // entries kept per part for rows
 constexpr int FCAP = 1024;                     // candidates a part or a row merges
 constexpr int FRCAP = 128;                     // entries of a part record
 constexpr int FMAXP = 16;                      // parts of one row (record slots)
-constexpr int FMAXT = (int)((int64_t)VINFER_MAX_VOCAB * 4 / FTILE);  // tiles of the longest row
+constexpr int FMAXT = (int)(((int64_t)VINFER_MAX_VOCAB * 4 + FTILE - 1) / FTILE);  // longest row
 constexpr size_t FREC_STRIDE = sizeof(RecHdr) + 8 * FRCAP;
 constexpr int FQ_HDR = 4;                      // deferred-row queue: pushed, claimed, CTAs done
-static_assert(FSTAGES % FW == 0 && FSTAGES >= 2 * FW, "each consumer has two stages");
-static_assert(FVPL == 16, "a consumer lane takes sixteen vectors of a tile");
+// Stage i % FSTAGES holds tile i and tile i goes to warp i % FW, so with FSTAGES a multiple of
+// FW every stage belongs to one warp, which waits on its phases in order. (A stage shared by two
+// warps would let one wait for a phase two ahead of the barrier's, which a one-bit phase parity
+// reports as complete.)
+static_assert(FSTAGES % FW == 0 && FSTAGES >= 2 * FW, "each consumer owns two stages");
+static_assert(FVPL * 32 * 16 == FTILE && FVPL <= 32, "a consumer lane takes FVPL vectors");
 static_assert(FKF + 64 <= FWB - 32, "a tightened list leaves room for a round of appends");
 static_assert(KC <= FSUMK && FSUMK <= FRCAP && FKF <= FRCAP, "records hold the kept entries");
 
@@ -76,8 +82,8 @@ struct __align__(16) FSlot {
 
 struct __align__(128) FSmem {
   unsigned char stage[FSTAGES][FTILE];         // the ring; after streaming, Smem for exact_row
-  FSlot slot[2];
-  unsigned long long wbuf[2][FW][FWB];         // consumer candidate lists, per slot
+  FSlot slot[FNSLOT];
+  unsigned long long wbuf[FNSLOT][FW][FWB];    // consumer candidate lists, per slot
   struct Fin {                                 // one finisher warp's scratch
     unsigned long long cand[FCAP];             // a part's candidates; a row's records
     unsigned long long srt[FCAP];              // ... sorted
@@ -86,9 +92,9 @@ struct __align__(128) FSmem {
   } fin[FNFIN];
   unsigned long long full[FSTAGES];            // mbarriers: tile landed
   unsigned long long empty[FSTAGES];           // ... consumer done with the stage
-  unsigned long long ready[2];                 // ... slot prepared (producer)
-  unsigned long long handed[2];                // ... all consumers done with the part
-  unsigned long long done[2];                  // ... finisher done with the part
+  unsigned long long ready[FNSLOT];            // ... slot prepared (prep warp)
+  unsigned long long handed[FNSLOT];           // ... all consumers done with the part
+  unsigned long long done[FNSLOT];             // ... finisher done with the part
   unsigned long long hbar;                     // ... history copy landed (producer)
   unsigned long long fin_all;                  // ... finisher done with every part
   int abort_, claim;
@@ -107,14 +113,16 @@ __device__ __forceinline__ void mbar_init(unsigned long long* b, uint32_t count)
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(b)), "r"(count)
                : "memory");
 }
+// one test of a barrier phase; a waiting thread is suspended for up to about 20 us (it resumes
+// as soon as the phase completes), so waiting warps do not spin on the issue slots
 __device__ __forceinline__ bool mbar_try_wait(unsigned long long* b, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_addr(b)), "r"(parity)
+      : "r"(smem_addr(b)), "r"(parity), "r"(20000u)
       : "memory");
   return ok != 0u;
 }
@@ -459,6 +467,47 @@ __device__ __forceinline__ void fw_scalar(FWarp& W, const FRow& r, FSlot* L, boo
   W.wc += __popc(m);
 }
 
+// Post this warp's lane values for the part's first bound and count the warp in; with
+// `wait`, wait (bounded) for all warps and raise the bound to the K-th largest posted value.
+__device__ __noinline__ void fw_post(FSlot* L, uint32_t lk) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  L->fmax[w * 32 + lane] = lk;
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence_block();
+    atomicAdd(&L->nfirst, 1);
+  }
+  __syncwarp();
+}
+__device__ __noinline__ FBound fw_first_wait(FSlot* L, FBound b, int K, float T, bool greedy) {
+  const int lane = threadIdx.x & 31;
+  int ready = 0;
+  if (lane == 0) {
+    for (int it = 0; it < (1 << 16); ++it) {
+      if (*reinterpret_cast<volatile int*>(&L->nfirst) >= FW) {
+        ready = 1;
+        break;
+      }
+      __nanosleep(32);
+    }
+    __threadfence_block();
+  }
+  // a warp that gave up keeps its own bound (a looser filter, never a wrong one)
+  if (!__shfl_sync(FULLMASK, ready, 0)) return b;
+  uint32_t ka[FW];
+#pragma unroll
+  for (int i = 0; i < FW; ++i) ka[i] = *reinterpret_cast<volatile uint32_t*>(&L->fmax[i * 32 + lane]);
+  const uint32_t va = warp_kth_hi(ka, K);
+  if (va != 0u) b = fw_publish(va, b, T, greedy, L);
+  return b;
+}
+__device__ __forceinline__ void fw_first_bound(FWarp& W, const FRow& r, FSlot* L, uint32_t lk) {
+  fw_post(L, lk);
+  const FBound b = fw_first_wait(L, FBound{W.tkey, W.th}, r.K, r.T, r.greedy);
+  W.tkey = b.tkey;
+  W.th = b.th;
+}
+
 // ---- one tile (one consumer warp) ----------------------------------------------------------------
 template <typename TIn, bool SUM>
 __device__ __forceinline__ void fused_tile(const KParams& P, FSlot* L, const FRow& r, bool first,
@@ -514,7 +563,7 @@ __device__ __forceinline__ void fused_tile(const KParams& P, FSlot* L, const FRo
       fw_scalar<SUM>(W, r, L, ok, y, (int)(P.voff + li), m_t, s_t);
     }
   }
-  // 3. the vectors: sixteen per lane
+  // 3. the vectors: FVPL per lane
   const uint4* sv = reinterpret_cast<const uint4*>(st);
   float vm[FVPL];
   float lmax = -INFINITY;
@@ -536,48 +585,26 @@ __device__ __forceinline__ void fused_tile(const KParams& P, FSlot* L, const FRo
     }
     lmax = fmaxf(lmax, vm[i]);
   }
-  if (first && r.K <= 32) {
-    // The part's first bounds, from the lanes' maxima (each the largest of 128 elements). This
-    // warp's: the K-th largest of its 32. Then the last warp to get here takes the K-th largest
-    // of all eight warps' 256, a bound from eight tiles' worth of elements.
+  if (first && r.K <= FKF) {
+    // The part's first bound: the K-th largest of the lanes' maxima of every warp's first tile
+    // (256 values, each the largest of 128 elements, K distinct elements reach it), so the
+    // first tile is filtered with a bound from eight tiles' worth of elements. Every warp
+    // posts its lanes' maxima and waits for the others (warps without a tile in the part post
+    // nothing and count at once), then takes the K-th itself.
     const uint32_t lk = lmax >= -FLT_MAX ? okey(lmax) : 0u;
-    const int w = threadIdx.x >> 5;
-    L->fmax[w * 32 + lane] = lk;
-    uint32_t one[1] = {lk};
-    const uint32_t kr = warp_kth_hi(one, r.K);
-    if (kr != 0u) {
-      const FBound bb = fw_publish(kr, FBound{W.tkey, W.th}, r.T, r.greedy, L);
-      W.tkey = bb.tkey;
-      W.th = bb.th;
-    }
-    __syncwarp();
-    int arrived = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      arrived = atomicAdd(&L->nfirst, 1);
-    }
-    arrived = __shfl_sync(FULLMASK, arrived, 0);
-    if (arrived == FW - 1) {
-      __threadfence_block();
-      uint32_t ka[FW];
+    fw_first_bound(W, r, L, lk);
+    if (W.th == -FLT_MAX) {
+      // too few posted values for K (a part of one or two tiles): the K-th largest of this
+      // warp's own vector maxima
+      uint32_t kk[FVPL];
 #pragma unroll
-      for (int i = 0; i < FW; ++i) ka[i] = *reinterpret_cast<volatile uint32_t*>(&L->fmax[i * 32 + lane]);
-      const uint32_t va = warp_kth_hi(ka, r.K);
-      if (va != 0u) {
-        const FBound bb = fw_publish(va, FBound{W.tkey, W.th}, r.T, r.greedy, L);
+      for (int i = 0; i < FVPL; ++i) kk[i] = vm[i] >= -FLT_MAX ? okey(vm[i]) : 0u;
+      const uint32_t vr = warp_kth_hi(kk, r.K);
+      if (vr != 0u) {
+        const FBound bb = fw_publish(vr, FBound{W.tkey, W.th}, r.T, r.greedy, L);
         W.tkey = bb.tkey;
         W.th = bb.th;
       }
-    }
-  } else if (first && r.K <= FKF) {  // larger K: the K-th largest of this warp's vector maxima
-    uint32_t kk[FVPL];
-#pragma unroll
-    for (int i = 0; i < FVPL; ++i) kk[i] = vm[i] >= -FLT_MAX ? okey(vm[i]) : 0u;
-    const uint32_t vr = warp_kth_hi(kk, r.K);
-    if (vr != 0u) {
-      const FBound bb = fw_publish(vr, FBound{W.tkey, W.th}, r.T, r.greedy, L);
-      W.tkey = bb.tkey;
-      W.th = bb.th;
     }
   }
   // 4. the elements of the vectors whose maximum reaches the filter (read again from the stage;
@@ -612,8 +639,34 @@ __device__ __forceinline__ void fused_tile(const KParams& P, FSlot* L, const FRo
     pos = warp_excl(n, &tot);
   }
   if (W.wc + tot > FWB) {
-    W.ovf = true;
-    return;
+    // the list cannot take this tile (a weak bound, and fewer than K entries to tighten on):
+    // raise the bound to the K-th largest of this tile's own vector maxima
+    uint32_t kk[FVPL];
+#pragma unroll
+    for (int i = 0; i < FVPL; ++i) kk[i] = vm[i] >= -FLT_MAX ? okey(vm[i]) : 0u;
+    const uint32_t vr = warp_kth_hi(kk, r.K);
+    if (vr != 0u) {
+      const FBound bb = fw_publish(vr, FBound{W.tkey, W.th}, r.T, r.greedy, L);
+      W.tkey = bb.tkey;
+      W.th = bb.th;
+      fw_tighten_now(W, r, L);  // the list's entries below the raised filter go
+      vbits = 0u;
+      n = 0;
+#pragma unroll
+      for (int i = 0; i < FVPL; ++i) {
+        if (vm[i] >= W.th) {
+          vbits |= 1u << i;
+          const uint4 q = sv[i * 32 + lane];
+#pragma unroll
+          for (int e = 0; e < A; ++e) n += E::at(q, e) >= W.th ? 1 : 0;
+        }
+      }
+      pos = warp_excl(n, &tot);
+    }
+    if (W.wc + tot > FWB) {
+      W.ovf = true;
+      return;
+    }
   }
   pos += W.wc;
   const float th = W.th;
@@ -753,6 +806,28 @@ __device__ void fused_prepare(const KParams& P, FSmem& S, FSlot& L, const FPartG
 
 template <typename TIn>
 __device__ void fused_producer(const KParams& P, FSmem& S) {
+  const int64_t g0 = ftile0(P, blockIdx.x), g1 = ftile0(P, blockIdx.x + 1);
+  if ((threadIdx.x & 31) != 0) return;
+  int row = -1;
+  int64_t rbase = 0;
+  for (int64_t g = g0; g < g1; ++g) {
+    const int i = (int)(g - g0);
+    const int s = i % FSTAGES;
+    if (!fwait(P, S, &S.empty[s], ((uint32_t)(i / FSTAGES) & 1u) ^ 1u)) return;
+    if (row < 0 || g - rbase >= P.ntr) {
+      row = (int)(g / P.ntr);
+      rbase = (int64_t)row * P.ntr;
+    }
+    const FTileGeo t = ftile<TIn>(P, row, (int)(g - rbase));
+    mbar_arrive_tx(&S.full[s], t.bytes);
+    if (t.bytes) bulk_load(S.stage[s], t.src, t.bytes, &S.full[s]);
+  }
+}
+
+// The prep warp: each part's slot, ahead of the consumers (a slot is reused once the part
+// FNSLOT earlier in the range is finished).
+template <typename TIn>
+__device__ void fused_prep(const KParams& P, FSmem& S) {
   const int lane = threadIdx.x & 31;
   const int64_t g0 = ftile0(P, blockIdx.x), g1 = ftile0(P, blockIdx.x + 1);
   uint32_t hphase = 0u;
@@ -760,28 +835,15 @@ __device__ void fused_producer(const KParams& P, FSmem& S) {
   int64_t g = g0;
   while (g < g1) {
     const FPartGeo q = fpart(P, g, g1);
-    FSlot& L = S.slot[p & 1];
-    if (p >= 2 && !fwait(P, S, &S.done[p & 1], (uint32_t)((p - 2) >> 1) & 1u)) return;
-    fused_prepare<TIn>(P, S, L, q, hphase);
+    const int sl = p % FNSLOT;
+    if (p >= FNSLOT &&
+        !fwait(P, S, &S.done[sl], (uint32_t)((p - FNSLOT) / FNSLOT) & 1u))
+      return;
+    fused_prepare<TIn>(P, S, S.slot[sl], q, hphase);
     if (lane == 0) {
       __threadfence_block();
-      mbar_arrive(&S.ready[p & 1]);
+      mbar_arrive(&S.ready[sl]);
     }
-    int ok = 1;
-    if (lane == 0) {
-      for (; g < q.g1; ++g) {
-        const int i = (int)(g - g0);
-        const int s = i % FSTAGES;
-        if (!fwait(P, S, &S.empty[s], ((uint32_t)(i / FSTAGES) & 1u) ^ 1u)) {
-          ok = 0;
-          break;
-        }
-        const FTileGeo t = ftile<TIn>(P, q.row, (int)(g - (int64_t)q.row * P.ntr));
-        mbar_arrive_tx(&S.full[s], t.bytes);
-        if (t.bytes) bulk_load(S.stage[s], t.src, t.bytes, &S.full[s]);
-      }
-    }
-    if (!__shfl_sync(FULLMASK, ok, 0)) return;
     g = q.g1;
     ++p;
   }
@@ -796,8 +858,9 @@ __device__ void fused_consume(const KParams& P, FSmem& S) {
   int64_t g = g0;
   while (g < g1) {
     const FPartGeo q = fpart(P, g, g1);
-    FSlot& L = S.slot[p & 1];
-    fwait(P, S, &S.ready[p & 1], (uint32_t)(p >> 1) & 1u);
+    const int sl = p % FNSLOT;
+    FSlot& L = S.slot[sl];
+    fwait(P, S, &S.ready[sl], (uint32_t)(p / FNSLOT) & 1u);
     const FPart pt = fpart_cfg(P, L);
     FRow r;
     r.T = pt.c.T;
@@ -810,7 +873,7 @@ __device__ void fused_consume(const KParams& P, FSmem& S) {
     r.pen = pt.pen;
     r.pen_down = pt.pen_down;
     FWarp W;
-    W.buf = S.wbuf[p & 1][w];
+    W.buf = S.wbuf[sl][w];
     W.wc = 0;
     W.tkey = okey(-FLT_MAX);
     W.th = -FLT_MAX;
@@ -818,8 +881,11 @@ __device__ void fused_consume(const KParams& P, FSmem& S) {
     float m_t = -FLT_MAX, s_t = 0.f;
     // this warp's tiles of the part: range index i with i % FW == w
     const int ib = (int)(g - g0), ie = (int)(q.g1 - g0);
+    const int i0 = ib + ((w - ib) % FW + FW) % FW;
+    // without a tile here, count in for the part's first bound at once
+    if (i0 >= ie && pt.mode != FM_SKIP && pt.K <= FKF) fw_post(&L, 0u);
     bool first = true;
-    for (int i = ib + ((w - ib) % FW + FW) % FW; i < ie; i += FW) {
+    for (int i = i0; i < ie; i += FW) {
       const int s = i % FSTAGES;
       const bool landed = fwait(P, S, &S.full[s], (uint32_t)(i / FSTAGES) & 1u);
       if (landed && pt.mode != FM_SKIP) {
@@ -855,7 +921,7 @@ __device__ void fused_consume(const KParams& P, FSmem& S) {
       L.wc[w] = W.wc;
       L.wovf[w] = W.ovf ? 1 : 0;
       __threadfence_block();
-      mbar_arrive(&S.handed[p & 1]);
+      mbar_arrive(&S.handed[sl]);
     }
     g = q.g1;
     ++p;
@@ -1000,7 +1066,12 @@ __device__ __forceinline__ void part_end(const KParams& P, FSmem& S, FFinS& F, F
   const uint32_t rk = *reinterpret_cast<volatile uint32_t*>(&L.thr_raw);
   uint32_t flags = c.bad ? REC_BAD : 0u;
   if (pt.exact) flags |= REC_EXACT;
-  for (int w = 0; w < FW; ++w) flags |= L.wovf[w] ? REC_OVERFLOW : 0u;
+  uint32_t why = 0u;  // diagnostics: 1 a warp's list overflowed, 2 too many candidates, 4 ties
+  for (int w = 0; w < FW; ++w)
+    if (L.wovf[w]) {
+      flags |= REC_OVERFLOW;
+      why |= 1u;
+    }
   int n = 0;  // candidates in F.srt
   uint32_t ck = tk;
   if (!(flags & (REC_BAD | REC_EXACT | REC_OVERFLOW))) {
@@ -1019,7 +1090,10 @@ __device__ __forceinline__ void part_end(const KParams& P, FSmem& S, FFinS& F, F
       }
     }
     __syncwarp();
-    if (n > FCAP) flags |= REC_OVERFLOW;
+    if (n > FCAP) {
+      flags |= REC_OVERFLOW;
+      why |= 2u;
+    }
   }
   // 2. keep the K largest (and ties of the K-th), sorted
   int nrec = 0;
@@ -1042,6 +1116,7 @@ __device__ __forceinline__ void part_end(const KParams& P, FSmem& S, FFinS& F, F
     }
     if (n > 128) {
       flags |= REC_OVERFLOW;  // ties of the Kk-th fill more than a record
+      why |= 4u;
     } else {
       if (n <= 64) warp_sort_smem<2>(F.srt, n);
       else warp_sort_smem<4>(F.srt, n);
@@ -1074,7 +1149,9 @@ __device__ __forceinline__ void part_end(const KParams& P, FSmem& S, FFinS& F, F
     h.n = nrec;
     // elements of the part may be missing from the list below its completeness key
     h.flags = flags | ((ck > okey(-FLT_MAX)) ? REC_UNRETAINED : 0u);
-    h.pad[0] = h.pad[1] = h.pad[2] = 0;
+    h.pad[0] = (int)why;
+    h.pad[1] = n;
+    h.pad[2] = 0;
     *reinterpret_cast<RecHdr*>(rec) = h;
   }
   __syncwarp();
@@ -1109,6 +1186,9 @@ __device__ __forceinline__ void row_finish(const KParams& P, FFinS& F, int row, 
     r.t_key = __ldcg(&h->t_key);
     r.n = __ldcg(&h->n);
     r.flags = __ldcg(&h->flags);
+    r.pad[0] = __ldcg(&h->pad[0]);
+    r.pad[1] = __ldcg(&h->pad[1]);
+    r.pad[2] = 0;
     F.ph[lane] = r;
   }
   __syncwarp();
@@ -1142,6 +1222,11 @@ __device__ __forceinline__ void row_finish(const KParams& P, FFinS& F, int row, 
     return;
   }
   bool undecided = (fl & (REC_OVERFLOW | REC_EXACT)) != 0 || tot > FCAP;
+  // why (diagnostics): 1 a part's lists overflowed, 2 a part needs the exact search, 4 too many
+  // entries to merge, 8 the K-th misses a part's completeness key, 16 fewer than K entries
+  uint32_t why = ((fl & REC_OVERFLOW) ? 1u : 0u) | ((fl & REC_EXACT) ? 2u : 0u) |
+                 (tot > FCAP ? 4u : 0u);
+  for (int p = 0; p < np; ++p) why |= (uint32_t)F.ph[p].pad[0] << 8;
   unsigned long long* e = F.srt;
   if (!undecided) {
     // every part's sorted entries into cand, then merged by rank into srt
@@ -1173,16 +1258,23 @@ __device__ __forceinline__ void row_finish(const KParams& P, FFinS& F, int row, 
     if (tot >= K) {
       kkey = comp_key(e[K - 1]);
       nk = count_ge(e, tot, kkey);
-      if (kkey < d) undecided = true;
+      if (kkey < d) {
+        undecided = true;
+        why |= 8u;
+      }
     } else if (d > okey(-FLT_MAX)) {
       undecided = true;
+      why |= 16u;
     }
   }
   if (local) {  // this rank's shard record
     RecHdr* oh = reinterpret_cast<RecHdr*>(shard);
     unsigned long long* oe = reinterpret_cast<unsigned long long*>(shard + sizeof(RecHdr));
     if (undecided) {
-      if (lane == 0) write_flag_hdr(oh, REC_OVERFLOW, m_y, s_y);
+      if (lane == 0) {
+        write_flag_hdr(oh, REC_OVERFLOW, m_y, s_y);
+        oh->pad[0] = (int)why;  // diagnostics only: why the shard's candidates do not decide
+      }
       return;
     }
     // rows with top-k: the K largest and the ties of the K-th; rows without: as many of the
@@ -1234,7 +1326,7 @@ __device__ __forceinline__ void row_finish(const KParams& P, FFinS& F, int row, 
 }
 
 // ---- the finisher warps ---------------------------------------------------------------------------
-// Finisher f takes the parts of parity f (slot f), so two parts can be finished at once.
+// Finisher f takes the parts p with p % FNFIN == f, so FNFIN parts can be finished at once.
 template <typename TIn>
 __device__ void fused_finish(const KParams& P, FSmem& S, int f) {
   const int64_t g0 = ftile0(P, blockIdx.x), g1 = ftile0(P, blockIdx.x + 1);
@@ -1243,12 +1335,13 @@ __device__ void fused_finish(const KParams& P, FSmem& S, int f) {
   int64_t g = g0;
   while (g < g1) {
     const FPartGeo q = fpart(P, g, g1);
-    if ((p & 1) == f) {
-      FSlot& L = S.slot[f];
-      if (fwait(P, S, &S.handed[f], (uint32_t)(p >> 1) & 1u))
-        part_end<TIn>(P, S, S.fin[f], L, &S.wbuf[f][0][0], q);
+    if (p % FNFIN == f) {
+      const int sl = p % FNSLOT;
+      FSlot& L = S.slot[sl];
+      if (fwait(P, S, &S.handed[sl], (uint32_t)(p / FNSLOT) & 1u))
+        part_end<TIn>(P, S, S.fin[f], L, &S.wbuf[sl][0][0], q);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&S.done[f]);
+      if (lane == 0) mbar_arrive(&S.done[sl]);
     }
     g = q.g1;
     ++p;
@@ -1267,7 +1360,7 @@ __global__ void __launch_bounds__(FNT, 1) k_fused(const __grid_constant__ KParam
       mbar_init(&S.full[s], 1u);
       mbar_init(&S.empty[s], 1u);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < FNSLOT; ++s) {
       mbar_init(&S.ready[s], 1u);
       mbar_init(&S.handed[s], (uint32_t)FW);
       mbar_init(&S.done[s], 1u);
@@ -1280,6 +1373,10 @@ __global__ void __launch_bounds__(FNT, 1) k_fused(const __grid_constant__ KParam
   __syncthreads();
   if (w == FPROD) {
     fused_producer<TIn>(P, S);
+    return;
+  }
+  if (w == FPREP) {
+    fused_prep<TIn>(P, S);
     return;
   }
   if (w >= FFIN) {
