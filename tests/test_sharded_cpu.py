@@ -5,12 +5,18 @@ all-gather delivered them in rank order, answers resolved rows from the CPU orac
 row, and flags chosen rows as unresolved. The tests check that every rank returns the same ids,
 that they equal the oracle's, and that the fallback rebuilt each unresolved row -- logits,
 parameters, uniform and history -- exactly from the shards.
+
+Failure handling, made on the host: a rank that exits between steps (the survivors' next step
+must raise within the process group's timeout), and a rank that raises inside the fallback
+(every rank must raise, none may hang).
 """
 
 from __future__ import annotations
 
+import datetime
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -137,6 +143,84 @@ def test_sharded_host_logic_on_gloo_ranks(world, config, unresolved):
                        start_method="spawn")
     got = sorted(results.get() for _ in range(world))
     assert got == [(r, "ok") for r in range(world)], got
+
+
+class FailingFullKernels(FakeShardKernels):
+    """Stand-in whose unsharded fallback raises on one rank (after the rows' all-gather)."""
+
+    def __init__(self, w: Workload, unresolved_rows: set[int], failing_rank: int) -> None:
+        super().__init__(w, unresolved_rows)
+        self.failing_rank = failing_rank
+
+    def full(self, logits, params, uniforms, history, out, probs_out):
+        if dist.get_rank() == self.failing_rank:
+            raise RuntimeError("injected failure in the fallback")
+        super().full(logits, params, uniforms, history, out, probs_out)
+
+
+PG_TIMEOUT_S = 6
+
+
+def _failure_rank_main(rank: int, world: int, port: int, scenario: str, results) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=PG_TIMEOUT_S))
+    w = make(3, batch=4, vocab=600)
+    lo, hi = shard_range(600, world, rank)
+    shard = w.logits[:, lo:hi].contiguous()
+    params = RowParams.from_arrays("cpu", **w.param_arrays())
+    u = torch.from_numpy(w.uniforms)
+    hist = TokenHistogram.from_csr(w.hist_row_ptr, w.hist_ids, w.hist_counts, "cpu")
+    if scenario == "leave":
+        s = ShardedSampler(FakeShardKernels(w, set()), record_cap=8)
+        s.sample_batch(shard, params, u, hist, 600)  # one full step on every rank
+        if rank == world - 1:
+            results.put((rank, "left"))
+            os._exit(0)  # leaves between steps: no collective of its own is in flight
+        t0 = time.monotonic()
+        try:
+            s.sample_batch(shard, params, u, hist, 600)
+            results.put((rank, "no error"))
+        except Exception as exc:  # noqa: BLE001 -- the expected outcome
+            results.put((rank, f"raised after {time.monotonic() - t0:.1f}s: "
+                               f"{type(exc).__name__}"))
+        os._exit(0)  # the group lost a member: skip its teardown
+    else:  # "fallback": rank 1 raises inside the unsharded fallback
+        s = ShardedSampler(FailingFullKernels(w, {1, 2}, failing_rank=1), record_cap=8)
+        try:
+            s.sample_batch(shard, params, u, hist, 600)
+            results.put((rank, "no error"))
+        except Exception as exc:  # noqa: BLE001 -- the expected outcome
+            results.put((rank, f"raised: {exc}"))
+        dist.destroy_process_group()
+
+
+def _run_failure(world: int, scenario: str) -> list[tuple[int, str]]:
+    ctx = mp.get_context("spawn")
+    results = ctx.SimpleQueue()
+    t0 = time.monotonic()
+    mp.start_processes(_failure_rank_main, args=(world, _free_port(), scenario, results),
+                       nprocs=world, join=True, start_method="spawn")
+    out = sorted(results.get() for _ in range(world))
+    # every rank ended well within a few process-group timeouts: nobody hung
+    assert time.monotonic() - t0 < 60 + 3 * PG_TIMEOUT_S
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_a_rank_that_leaves_between_steps_fails_the_survivors_next_step(world):
+    got = _run_failure(world, "leave")
+    assert got[-1] == (world - 1, "left")
+    for rank, msg in got[:-1]:
+        assert msg.startswith("raised after"), (rank, msg)
+        # an error within the process group's timeout (plus scheduling slack), not a hang
+        assert float(msg.split()[2].rstrip("s:")) <= PG_TIMEOUT_S + 10, msg
+
+
+def test_a_rank_that_raises_in_the_fallback_fails_every_rank():
+    got = _run_failure(2, "fallback")
+    assert got[0][0] == 0 and "rank(s) failed while resolving rows [1, 2]" in got[0][1], got
+    assert got[1][0] == 1 and "injected failure in the fallback" in got[1][1], got
 
 
 def test_select_rows_rebuilds_histories():

@@ -171,7 +171,29 @@ class ShardedSampler:
         return out
 
     def _resolve(self, logits, params, uniforms, history, vocab_total, out, probs_out, idx):
-        """Assemble the full rows ``idx`` from every rank's shard and sample them unsharded."""
+        """Assemble the full rows ``idx`` from every rank's shard and sample them unsharded.
+
+        Ends with a status all-reduce that every rank reaches, so that a rank failing here after
+        the rows' all-gather makes every rank raise (the ranks would otherwise go on with
+        different ids). A rank failing before the all-gather leaves the others in it until the
+        process group's timeout ends it with an error."""
+        failed = None
+        try:
+            self._resolve_rows(logits, params, uniforms, history, vocab_total, out, probs_out,
+                               idx)
+        except Exception as exc:  # noqa: BLE001 -- reported to every rank below, then re-raised
+            failed = exc
+        status = torch.tensor([0 if failed is None else 1], dtype=torch.int32,
+                              device=logits.device)
+        dist.all_reduce(status, group=self.group)
+        if failed is not None:
+            raise failed
+        if int(status.item()):
+            raise RuntimeError(f"{int(status.item())} rank(s) failed while resolving rows "
+                               f"{idx.tolist()} from the full vocabulary")
+
+    def _resolve_rows(self, logits, params, uniforms, history, vocab_total, out, probs_out,
+                      idx):
         n, dev = idx.numel(), logits.device
         width = max(hi - lo for lo, hi in
                     (shard_range(vocab_total, self.world, r) for r in range(self.world)))
