@@ -444,6 +444,51 @@ def bench_single_config4(args) -> dict:
 # ----------------------------------------------------------------------------------------------
 # N > 1: configuration 4, vocab-sharded (one process per GPU, NCCL)
 # ----------------------------------------------------------------------------------------------
+def graphed(step, K: int):
+    """CUDA graphs of G = min(K, 64) calls of ``step(i)`` (and of K % G); replaying ``plan`` in
+    order runs K steps with no host launch cost."""
+    G = min(K, 64)
+    graphs = []
+    for n in ([G] if K % G == 0 else [G, K % G]):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                step(i)
+        graphs.append(g)
+    torch.cuda.synchronize()
+    return graphs, [graphs[0]] * (K // G) + ([graphs[1]] if K % G else []), G
+
+
+def unsharded_config4_rows_per_s(backend, dev, K: int) -> float:
+    """Configuration 4 on this one GPU, unsharded (batch 1024 x vocab 248,320), through
+    ``sample_batch`` in CUDA graphs: the strong-scaling reference of the sharded lines."""
+    from vinfer_b200.workloads import config4_shard  # noqa: PLC0415
+
+    B, V = 1024, 248_320
+    x, params, u = config4_shard(0, 1, dev, B, V)
+    nbuf = max(2, int(np.ceil(2 * L2_BYTES / (x.numel() * 2))) + 1)
+    bufs = [x] + [x.clone() for _ in range(nbuf - 1)]
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+
+    def step(i: int) -> None:
+        backend.sample_batch(bufs[i % nbuf], params, u, None, out=out)
+
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize()
+    graphs, plan, _ = graphed(step, K)
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for g in plan:
+        g.replay()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    backend.check()
+    del graphs, plan, bufs
+    return B * K / (t0.elapsed_time(t1) * 1e-3)
+
+
 def bench_sharded(args) -> dict | None:
     from datetime import timedelta  # noqa: PLC0415
 
@@ -457,6 +502,7 @@ def bench_sharded(args) -> dict | None:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    graphs = plan = None
     try:
         backend = SAMPLER.resolve("b200", BackendContext(dev, torch.bfloat16))
         sampler = ShardedSampler(B200ShardKernels(backend))
@@ -469,44 +515,67 @@ def bench_sharded(args) -> dict | None:
         out = torch.empty(B, dtype=torch.int32, device=dev)
         stream = torch.cuda.current_stream(dev)
 
+        # the device steps of one batch (local records, NCCL all-gather, merge): no host
+        # synchronisation, so K of them are replayed from CUDA graphs; the rows they leave
+        # unresolved are counted on the device and read once after the timed region
         def step(i: int) -> None:
-            sampler.sample_batch(bufs[i % nbuf], params, u, None, V, out=out)
+            sampler.sample_batch_async(bufs[i % nbuf], params, u, None, V, out=out)
 
         for i in range(max(args.warmup, 3)):
-            step(i)
+            sampler.sample_batch(bufs[i % nbuf], params, u, None, V, out=out)
         torch.cuda.synchronize()
         sampler.kernels.check()
+        sampler.pending_unresolved(dev)
+        graphs, plan, G = graphed(step, args.steps)
 
         clocks = Clocks(local) if rank == 0 else None
         if clocks:
             clocks.start()
-        unresolved = 0
         dist.barrier()
         torch.cuda.synchronize()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record(stream)
-        for i in range(args.steps):
-            step(i)
-            unresolved += sampler.last_unresolved
+        for g in plan:
+            g.replay()
         t1.record(stream)
         torch.cuda.synchronize()
         dist.barrier()
         ms = t0.elapsed_time(t1)
         clk = clocks.stop() if clocks else None
+        unresolved = sampler.pending_unresolved(dev)
+        sampler.kernels.check()
+        del graphs, plan  # graphs holding NCCL calls go before the process group
+        graphs = plan = None
 
-        # the local-record kernel alone: events around single launches on its stream
+        # phases of one step: events around each device step on the launching stream
         bufd = sampler._buffers(B, dev)
         torch.cuda._sleep(20_000_000)
-        pairs = []
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(16)]
         for i in range(16):
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record(stream)
+            ev[i][0].record(stream)
             sampler.kernels.local(bufs[i % nbuf], params, u, None, lo, V, sampler.record_cap,
                                   bufd["local"], bufd["scratch_ids"])
-            e.record(stream)
-            pairs.append((s, e))
+            ev[i][1].record(stream)
+            dist.all_gather_into_tensor(bufd["gathered"], bufd["local"])
+            ev[i][2].record(stream)
+            sampler.kernels.merge(bufs[i % nbuf], params, u, None, lo, V, sampler.record_cap,
+                                  bufd["gathered"], world, out, bufd["unresolved"], None)
+            ev[i][3].record(stream)
         torch.cuda.synchronize()
-        local_ms = statistics.mean(s.elapsed_time(e) for s, e in pairs)
+        phases = [statistics.mean(e[k].elapsed_time(e[k + 1]) for e in ev) for k in range(3)]
+        local_ms = phases[0]
+
+        # correctness of the timed configuration, checked on every rank: the same ids on all
+        # ranks, and 16 rows assembled in full and sampled unsharded give the sharded ids
+        ids = sampler.sample_batch(bufs[0], params, u, None, V, out=torch.empty_like(out))
+        allids = torch.empty(world * B, dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(allids, ids)
+        same = bool((allids.view(world, B) == ids.view(1, B)).all())
+        idx = torch.arange(16, device=dev) * (B // 16) + 7
+        spot = ids.clone()
+        spot[idx] = -1
+        sampler._resolve_rows(bufs[0], params, u, None, V, spot, None, idx)
+        spot_ok = bool(torch.equal(spot, ids))
 
         # end to end through the public API: this rank's shard and the row parameters copied
         # from pinned host memory, the ids copied back, every step
@@ -526,8 +595,8 @@ def bench_sharded(args) -> dict | None:
             for k, t in host_p.items():
                 getattr(params, k).copy_(t, non_blocking=True)
             d_u.copy_(host_u, non_blocking=True)
-            ids = sampler.sample_batch(d_x, params, d_u, None, V, out=out)
-            host_ids.copy_(ids, non_blocking=True)
+            r = sampler.sample_batch(d_x, params, d_u, None, V, out=out)
+            host_ids.copy_(r, non_blocking=True)
 
         e2e_steps = max(3, min(args.steps, 20))
         e2e_step()
@@ -542,20 +611,29 @@ def bench_sharded(args) -> dict | None:
         e2e_ms = e0.elapsed_time(e1) / e2e_steps
         sampler.kernels.check()
 
-        t = torch.tensor([ms, local_ms, e2e_ms, float(unresolved)], dtype=torch.float64,
-                         device=dev)
+        # the strong-scaling reference: configuration 4 unsharded on rank 0's GPU alone
+        ref = unsharded_config4_rows_per_s(backend, dev, args.steps) if rank == 0 else 0.0
+        dist.barrier()
+
+        t = torch.tensor([ms, local_ms, e2e_ms, float(unresolved), *phases,
+                          0.0 if same else 1.0, 0.0 if spot_ok else 1.0],
+                         dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, local_ms, e2e_ms, unresolved = float(t[0]), float(t[1]), float(t[2]), int(t[3])
+        phases = [float(v) for v in t[4:7]]
+        same, spot_ok = float(t[7]) == 0.0, float(t[8]) == 0.0
     finally:
+        del graphs, plan
         dist.destroy_process_group()
     if rank != 0:
         return None
     peak, kind = measured_peak()
     shard_algo = B * (hi - lo) * 2 + 36 * B  # local-record pass: this rank's logits and params
     achieved = shard_algo / (local_ms * 1e-3) / 1e9
+    value = B * args.steps / (ms * 1e-3)
     return {
         "metric": METRIC,
-        "value": B * args.steps / (ms * 1e-3),
+        "value": value,
         "unit": "rows/s",
         "n_gpus": world,
         "steps": args.steps,
@@ -573,7 +651,17 @@ def bench_sharded(args) -> dict | None:
                    "l2": f"{nbuf} rotating shard buffers per rank "
                          f"({nbuf * shard_bytes / 2**20:.0f} MiB > 2x L2)",
                    "parallelism": f"vocab-sharded over {world} ranks",
+                   "graph_steps": G,
                    "unresolved_rows_in_timed_steps": unresolved},
+        "strong_scaling_ref": {"value": ref, "unit": "rows/s",
+                               "what": "configuration 4 unsharded on one GPU (rank 0's), "
+                                       "sample_batch in CUDA graphs",
+                               "speedup": value / ref if ref else None},
+        "phase_ms": {"local_records": phases[0], "all_gather": phases[1], "merge": phases[2],
+                     "how": "CUDA events around each device step, mean of 16 eager steps, "
+                            "max over ranks"},
+        "ids_equal_across_ranks": same,
+        "spot_rows_match": spot_ok,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": f"{kind} (copy bandwidth)",
                      "traffic": None, "algorithmic_bytes": shard_algo,

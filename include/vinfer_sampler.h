@@ -53,9 +53,6 @@ extern "C" {
 /* bits OR-ed into *status by the device */
 #define VINFER_ST_BAD_PARAM 1u   /* a row's parameters are invalid; its id is -1 */
 #define VINFER_ST_NONFINITE 2u   /* a row has no finite maximum after processing */
-#define VINFER_ST_TIMEOUT 4u     /* a bounded wait gave up (a copy that never landed, a stage
-                                    never freed): the call's results are not valid; re-initialise
-                                    the workspace before the next call */
 #define VINFER_ST_INTERNAL 8u    /* an internal consistency check failed */
 
 /* args.flags */
@@ -97,8 +94,8 @@ int vinfer_sampler_abi_version(void);
 
 /* Workspace bytes `vinfer_sample` needs for this shape (independent of the device). A workspace
  * of N bytes serves every shape whose size is at most N: it starts with a header whose place and
- * size do not depend on the shape (per-row arrival counters for VINFER_MAX_BATCH rows and the
- * queue of rows searched exactly), which every call leaves at zero. */
+ * size do not depend on the shape (per-row arrival counters for VINFER_MAX_BATCH rows), which
+ * every call leaves at zero. */
 size_t vinfer_sampler_workspace_bytes(int64_t batch, int64_t vocab, int32_t dtype);
 
 /* Zero a workspace once after allocating it; calls leave it ready for the next call, of any
@@ -133,8 +130,7 @@ int vinfer_sample_merge(const VinferSampleArgs* args, int32_t record_cap, const 
  * fixed array of VINFER_STATIC_SCRATCH_BYTES compiled into the library, which every device
  * that loads the library holds until the process exits. It allocates nothing.
  *  - Limit: the call returns VINFER_E_LIMIT when vinfer_sampler_workspace_bytes(batch, vocab,
- *    dtype) exceeds VINFER_STATIC_SCRATCH_BYTES (any batch of up to 15,405 rows fits at any
- *    vocabulary).
+ *    dtype) exceeds VINFER_STATIC_SCRATCH_BYTES (at least 63 rows fit at any vocabulary).
  *  - The first call on a device looks up the array's device address on that device (which
  *    may load the library's device code); make it before any stream capture. The address is
  *    kept for the life of the process: the library does not survive a cudaDeviceReset (or any

@@ -122,6 +122,15 @@ def _rank_main(rank: int, world: int, port: int, config: int, batch: int, vocab:
         gathered = [None] * world
         dist.all_gather_object(gathered, ids.tolist())
         assert all(g == gathered[0] for g in gathered)
+        # the device steps alone: no fallback, unresolved rows left at -1 and counted
+        s.pending_unresolved(shard.device)
+        for _ in range(2):
+            ids2 = s.sample_batch_async(shard, params, u, hist, vocab)
+        assert s.pending_unresolved(shard.device) == 2 * len(unresolved)
+        assert s.pending_unresolved(shard.device) == 0
+        keep = [r for r in range(w.batch) if r not in unresolved]
+        assert np.array_equal(ids2.numpy()[keep], want[keep])
+        assert all(int(ids2[r]) == -1 for r in unresolved)
         results.put((rank, "ok"))
     except Exception as exc:  # reported to the parent, which fails the test
         results.put((rank, repr(exc)))

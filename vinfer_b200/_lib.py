@@ -17,7 +17,7 @@ ABI_VERSION = 1
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 OK, E_ARG, E_LIMIT, E_CUDA = 0, 1, 2, 3
-ST_BAD_PARAM, ST_NONFINITE, ST_TIMEOUT, ST_INTERNAL = 1, 2, 4, 8
+ST_BAD_PARAM, ST_NONFINITE, ST_INTERNAL = 1, 2, 8
 FLAG_EXACT_ALL = 1
 MAX_VOCAB = 262144
 MAX_BATCH = 65535
@@ -116,8 +116,6 @@ def status_message(bits: int) -> str:
         names.append("invalid sampling parameters in a row")
     if bits & ST_NONFINITE:
         names.append("a row has no finite logit")
-    if bits & ST_TIMEOUT:
-        names.append("a bounded wait timed out")
     if bits & ST_INTERNAL:
         names.append("internal consistency check failed")
     return ", ".join(names) or "ok"

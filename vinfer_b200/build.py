@@ -19,7 +19,7 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libvinfer_sampler.so"
 SOURCES = [CSRC / "sampler.cu"]
-HEADERS = [INCLUDE / "vinfer_sampler.h", CSRC / "fused.cuh"]
+HEADERS = [INCLUDE / "vinfer_sampler.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

@@ -121,12 +121,6 @@ struct KParams {
   unsigned char* shard_out;
   int shard_cap;
   size_t shard_stride;
-  // the fused pass (k_fused): tiles of te elements, ntr per row, ntt in the batch, streamed by
-  // geff CTAs in equal contiguous ranges; part records in `slots` slots per row (at recs); the
-  // deferred-row queue
-  int te, ntr, geff, slots;
-  int64_t ntt;
-  int* queue;
 };
 
 struct __align__(16) Smem {
@@ -2816,61 +2810,60 @@ __global__ void __launch_bounds__(256) k_probs(const __grid_constant__ KParams P
   }
 }
 
-#include "fused.cuh"
-
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
+struct Shape {
+  int nseg, seg_len, grid;
+};
+
+// Segments per row and CTAs for a batch. A row is cut into at least enough segments of at most
+// SEG_BYTES. When the batch has fewer rows than the device has resident CTAs, each row is cut
+// into c = ctas / B runs of whole segments (nseg a multiple of c, segments of at least 2048
+// tokens), so every CTA streams one run; with as many rows as CTAs or more, the CTAs share the
+// row-major list of segments in equal contiguous ranges. One run per CTA pays the per-run
+// set-up once and leaves SM room for the finishing kernel to start early.
+Shape plan(int64_t B, int64_t V, int dtype, int ctas) {
+  const int es = dtype == VINFER_DTYPE_BF16 ? 2 : 4;
+  const int A = 16 / es;
+  const int64_t min_seg = (V * es + SEG_BYTES - 1) / SEG_BYTES;
+  int64_t c = 1;
+  if (B < ctas) c = std::min<int64_t>(ctas / B, MAX_NSEG);
+  c = std::max<int64_t>(1, std::min<int64_t>(c, V / 2048));
+  int64_t nseg = std::max<int64_t>(min_seg, c);
+  nseg = (nseg + c - 1) / c * c;
+  nseg = std::min<int64_t>(nseg, MAX_NSEG);
+  int64_t len = (V + nseg - 1) / nseg;
+  len = (len + A - 1) / A * A;
+  nseg = (V + len - 1) / len;
+  Shape s;
+  s.nseg = (int)nseg;
+  s.seg_len = (int)len;
+  s.grid = (int)std::min<int64_t>(B * nseg, B < ctas ? B * c : ctas);
+  return s;
+}
+
 constexpr size_t ALIGN = 256;
 size_t align_up(size_t x) { return (x + ALIGN - 1) / ALIGN * ALIGN; }
 
-// Every workspace starts with a header whose place and size do not depend on the shape: the
-// per-row arrival counters for the largest batch, then the deferred-row queue. A workspace used
-// for calls of different shapes therefore never finds another call's records over its counters;
-// every call leaves the counters and the queue at zero.
-constexpr size_t HDR_QUEUE = ((size_t)VINFER_MAX_BATCH * 4 + ALIGN - 1) / ALIGN * ALIGN;
-constexpr size_t HDR_BYTES =
-    (HDR_QUEUE + (size_t)(FQ_HDR + VINFER_MAX_BATCH) * 4 + ALIGN - 1) / ALIGN * ALIGN;
-
-struct FShape {
-  int te, ntr, geff, slots;
-  int64_t ntt;
-};
-int elem_size(int dtype) { return dtype == VINFER_DTYPE_BF16 ? 2 : 4; }
-
-// Record slots per row: a row meets at most ceil(ntr / tpc) + 1 CTAs when every CTA streams at
-// least tpc tiles. The plan below gives every CTA at least ceil(ntr / (FMAXP - 1)) tiles, and at
-// least ntt / CTA_CAP as no device runs more CTAs; the bound holds on any device.
-int fslots(int64_t B, int64_t V, int dtype) {
-  const int64_t te = FTILE / elem_size(dtype);
-  const int64_t ntr = (V + te - 1) / te, ntt = B * ntr;
-  const int64_t tpc = std::max<int64_t>({(ntr + FMAXP - 2) / (FMAXP - 1), ntt / CTA_CAP, 1});
-  return (int)std::min<int64_t>(FMAXP, (ntr + tpc - 1) / tpc + 1);
-}
-// The fused pass over a batch on a device with `ctas` resident CTAs: CTAs take equal
-// contiguous ranges of the row-major tile list, at least ceil(ntr / (FMAXP - 1)) tiles each.
-FShape fplan(int64_t B, int64_t V, int dtype, int ctas) {
-  FShape f;
-  f.te = FTILE / elem_size(dtype);
-  f.ntr = (int)((V + f.te - 1) / f.te);
-  f.ntt = B * f.ntr;
-  const int64_t tpc_min = (f.ntr + FMAXP - 2) / (FMAXP - 1);
-  f.geff = (int)std::max<int64_t>(1, std::min<int64_t>({(int64_t)ctas, (int64_t)CTA_CAP,
-                                                        f.ntt / tpc_min}));
-  f.slots = fslots(B, V, dtype);
-  return f;
-}
+// Every workspace starts with the per-row arrival counters for the largest batch, whose place
+// and size do not depend on the shape: a workspace used for calls of different shapes never
+// finds another call's records over its counters, and every call leaves them at zero.
+constexpr size_t HDR_BYTES = ((size_t)VINFER_MAX_BATCH * 4 + ALIGN - 1) / ALIGN * ALIGN;
 
 struct WsLayout {
-  size_t counters, queue, rows, recs, total;
+  size_t counters, rows, recs, total;
 };
+// Records: one slot per (row, run); a row has at most nseg runs. Below the resident-CTA bound
+// rows may be split up to MAX_NSEG ways, depending on the device; from it on, the segment size
+// alone sets nseg. Either way the size does not depend on the device.
 WsLayout ws_layout(int64_t B, int64_t V, int dtype) {
+  const int64_t nseg = B < CTA_CAP ? MAX_NSEG : plan(B, V, dtype, CTA_CAP).nseg;
   WsLayout L;
   L.counters = 0;
-  L.queue = HDR_QUEUE;
   L.rows = HDR_BYTES;
   L.recs = L.rows + align_up((size_t)B * sizeof(RowState));
-  L.total = L.recs + (size_t)B * fslots(B, V, dtype) * FREC_STRIDE;
+  L.total = L.recs + (size_t)B * nseg * REC_STRIDE;
   return L;
 }
 
@@ -2887,7 +2880,7 @@ int check_args(const VinferSampleArgs* a) {
   return VINFER_OK;
 }
 
-KParams make_params(const VinferSampleArgs* a, void* ws) {
+KParams make_params(const VinferSampleArgs* a, const Shape& s, void* ws) {
   KParams P = {};
   P.logits = a->logits;
   P.ld = a->ld;
@@ -2895,6 +2888,10 @@ KParams make_params(const VinferSampleArgs* a, void* ws) {
   P.voff = a->vocab_offset;
   P.vtotal = a->vocab_total;
   P.B = (int)a->batch;
+  P.nseg = s.nseg;
+  P.seg_len = s.seg_len;
+  P.total = (int)(a->batch * s.nseg);
+  P.grid = s.grid;
   P.flags = a->flags;
   P.temperature = a->temperature;
   P.top_k = a->top_k;
@@ -2913,7 +2910,6 @@ KParams make_params(const VinferSampleArgs* a, void* ws) {
   const WsLayout L = ws_layout(a->batch, a->vocab, a->dtype);
   unsigned char* base = (unsigned char*)ws;
   P.counters = (int*)(base + L.counters);
-  P.queue = (int*)(base + L.queue);
   P.rows = (RowState*)(base + L.rows);
   P.recs = base + L.recs;
   return P;
@@ -2927,7 +2923,7 @@ struct KernInfo {
 };
 std::mutex g_info_mu;
 int kernel_info(const void* kern, int slot, int threads, size_t smem, int* ctas) {
-  static KernInfo info[64][4] = {};
+  static KernInfo info[64][6] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VINFER_E_CUDA;
   std::lock_guard<std::mutex> lock(g_info_mu);
@@ -2949,21 +2945,39 @@ int kernel_info(const void* kern, int slot, int threads, size_t smem, int* ctas)
   return VINFER_OK;
 }
 
-// the fused pass: mode 0 answers every row, mode 1 writes this rank's shard records
-int launch_fused(KParams& P, int dtype, cudaStream_t st) {
+// resident CTAs of k_stream on the current device (at most CTA_CAP)
+int sample_ctas(int dtype, int* ctas) {
+  const void* kern = dtype == VINFER_DTYPE_BF16 ? (const void*)k_stream<__nv_bfloat16>
+                                                : (const void*)k_stream<float>;
+  if (kernel_info(kern, dtype == VINFER_DTYPE_BF16 ? 0 : 1, NT, sizeof(Smem), ctas) != VINFER_OK)
+    return VINFER_E_CUDA;
+  *ctas = std::min(*ctas, CTA_CAP);
+  return VINFER_OK;
+}
+// k_stream, then k_finish (mode 0: every row's answer; mode 1: this rank's shard records)
+int launch_sample(const KParams& P, int dtype, cudaStream_t st) {
   const bool bf = dtype == VINFER_DTYPE_BF16;
-  const void* kern = bf ? (const void*)k_fused<__nv_bfloat16> : (const void*)k_fused<float>;
-  int ctas = 0;
-  if (kernel_info(kern, bf ? 0 : 1, FNT, sizeof(FSmem), &ctas) != VINFER_OK) return VINFER_E_CUDA;
-  const FShape f = fplan(P.B, P.V, dtype, ctas);
-  P.te = f.te;
-  P.ntr = f.ntr;
-  P.ntt = f.ntt;
-  P.geff = f.geff;
-  P.slots = f.slots;
-  if (bf) k_fused<__nv_bfloat16><<<f.geff, FNT, sizeof(FSmem), st>>>(P);
-  else k_fused<float><<<f.geff, FNT, sizeof(FSmem), st>>>(P);
-  return cudaGetLastError() == cudaSuccess ? VINFER_OK : VINFER_E_CUDA;
+  const void* fin = bf ? (const void*)k_finish<__nv_bfloat16> : (const void*)k_finish<float>;
+  int unused = 0;
+  if (kernel_info(fin, bf ? 4 : 5, NT, sizeof(Smem), &unused) != VINFER_OK) return VINFER_E_CUDA;
+  if (bf) k_stream<__nv_bfloat16><<<P.grid, NT, sizeof(Smem), st>>>(P);
+  else k_stream<float><<<P.grid, NT, sizeof(Smem), st>>>(P);
+  if (cudaGetLastError() != cudaSuccess) return VINFER_E_CUDA;
+  // programmatic dependent launch: k_finish starts on SMs as k_stream frees them and does its
+  // input-only set-up before waiting for k_stream's records
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)P.B);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = sizeof(Smem);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = bf ? cudaLaunchKernelEx(&cfg, k_finish<__nv_bfloat16>, P)
+                           : cudaLaunchKernelEx(&cfg, k_finish<float>, P);
+  return e == cudaSuccess ? VINFER_OK : VINFER_E_CUDA;
 }
 int launch_probs(const KParams& P, int dtype, cudaStream_t st) {
   if (!P.out_probs) return VINFER_OK;
@@ -3003,10 +3017,13 @@ int vinfer_sample(const VinferSampleArgs* a, void* workspace, size_t workspace_b
   if (a->vocab_offset != 0 || a->vocab_total != a->vocab) return VINFER_E_ARG;
   if (!workspace) return VINFER_E_ARG;
   if (workspace_bytes < ws_layout(a->batch, a->vocab, a->dtype).total) return VINFER_E_LIMIT;
-  KParams P = make_params(a, workspace);
+  int ctas = 0;
+  if (sample_ctas(a->dtype, &ctas) != VINFER_OK) return VINFER_E_CUDA;
+  const Shape s = plan(a->batch, a->vocab, a->dtype, ctas);
+  KParams P = make_params(a, s, workspace);
   P.mode = 0;
   cudaStream_t st = (cudaStream_t)stream;
-  rc = launch_fused(P, a->dtype, st);
+  rc = launch_sample(P, a->dtype, st);
   if (rc != VINFER_OK) return rc;
   return launch_probs(P, a->dtype, st);
 }
@@ -3022,12 +3039,15 @@ int vinfer_sample_local(const VinferSampleArgs* a, int32_t record_cap, void* rec
   if (rc != VINFER_OK) return rc;
   if (!records || !workspace || record_cap < 1 || record_cap > CAND_CAP) return VINFER_E_ARG;
   if (workspace_bytes < ws_layout(a->batch, a->vocab, a->dtype).total) return VINFER_E_LIMIT;
-  KParams P = make_params(a, workspace);
+  int ctas = 0;
+  if (sample_ctas(a->dtype, &ctas) != VINFER_OK) return VINFER_E_CUDA;
+  const Shape s = plan(a->batch, a->vocab, a->dtype, ctas);
+  KParams P = make_params(a, s, workspace);
   P.mode = 1;
   P.shard_out = (unsigned char*)records;
   P.shard_cap = record_cap;
   P.shard_stride = vinfer_sample_record_bytes(record_cap);
-  return launch_fused(P, a->dtype, (cudaStream_t)stream);
+  return launch_sample(P, a->dtype, (cudaStream_t)stream);
 }
 
 int vinfer_sample_merge(const VinferSampleArgs* a, int32_t record_cap, const void* records,
@@ -3040,7 +3060,8 @@ int vinfer_sample_merge(const VinferSampleArgs* a, int32_t record_cap, const voi
     return VINFER_E_ARG;
   if (world_size * record_cap > MERGE_CAP) return VINFER_E_LIMIT;
   if (workspace_bytes < ws_layout(a->batch, a->vocab, a->dtype).total) return VINFER_E_LIMIT;
-  KParams P = make_params(a, workspace);
+  const Shape s = plan(a->batch, a->vocab, a->dtype, 1);
+  KParams P = make_params(a, s, workspace);
   P.mode = 2;
   P.shard_cap = record_cap;
   P.shard_stride = vinfer_sample_record_bytes(record_cap);
@@ -3106,13 +3127,17 @@ int vinfer_sample_static(const VinferSampleArgs* a, void* stream) {
   void* ws = nullptr;
   if (static_scratch(&ws) != VINFER_OK) return VINFER_E_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
-  // The header (per-row arrival counters and the deferred-row queue) must start at zero. The
-  // array keeps whatever the previous call left; a call that gave up (a timeout) may have left
-  // it dirty, so clear it on every call.
-  if (cudaMemsetAsync(ws, 0, HDR_BYTES, st) != cudaSuccess) return VINFER_E_CUDA;
-  KParams P = make_params(a, ws);
+  // The per-row arrival counters must start at zero; the array keeps whatever the previous call
+  // left, so clear this call's counters.
+  if (cudaMemsetAsync((unsigned char*)ws + L.counters, 0, (size_t)a->batch * sizeof(int), st) !=
+      cudaSuccess)
+    return VINFER_E_CUDA;
+  int ctas = 0;
+  if (sample_ctas(a->dtype, &ctas) != VINFER_OK) return VINFER_E_CUDA;
+  const Shape s = plan(a->batch, a->vocab, a->dtype, ctas);
+  KParams P = make_params(a, s, ws);
   P.mode = 0;
-  rc = launch_fused(P, a->dtype, st);
+  rc = launch_sample(P, a->dtype, st);
   if (rc != VINFER_OK) return rc;
   return launch_probs(P, a->dtype, st);
 }

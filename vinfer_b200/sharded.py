@@ -123,6 +123,7 @@ class ShardedSampler:
         self.record_cap = record_cap
         self.rec_bytes = kernels.record_bytes(record_cap)
         self._bufs: dict = {}
+        self._totals: dict = {}
         self.last_unresolved = 0
 
     def _buffers(self, B: int, device: torch.device):
@@ -144,7 +145,31 @@ class ShardedSampler:
         """Sample one global token id per row from this rank's shard ``logits [B, V/w]``.
 
         ``probs_out`` (optional, ``[B, V/w]`` float32) receives this rank's slice of the final
-        probabilities."""
+        probabilities. The device steps (``sample_batch_async``), then one read of the
+        unresolved flags and, for the rare unresolved rows, the full-row fallback."""
+        out = self.sample_batch_async(logits, params, uniforms, history, vocab_total, out,
+                                      probs_out)
+        buf = self._buffers(logits.shape[0], logits.device)
+        # identical on every rank: all ranks take the fallback for the same rows. One boolean
+        # read per step (the count only when some row is unresolved, which is rare).
+        n = 0
+        if bool(buf["unresolved"].any()):
+            n = int(torch.count_nonzero(buf["unresolved"]))
+        self.last_unresolved = n
+        if n:
+            self._resolve(logits, params, uniforms, history, vocab_total, out, probs_out,
+                          torch.nonzero(buf["unresolved"]).flatten())
+        return out
+
+    def sample_batch_async(self, logits: torch.Tensor, params: RowParams,
+                           uniforms: torch.Tensor, history: TokenHistogram | None,
+                           vocab_total: int, out: torch.Tensor | None = None,
+                           probs_out: torch.Tensor | None = None) -> torch.Tensor:
+        """The device steps of ``sample_batch`` alone (local records, all-gather, merge), with
+        no host synchronisation, so that they can be captured in a CUDA graph. Rows the records
+        cannot decide are left at -1 in ``out`` and counted into ``unresolved_total`` (a device
+        tensor; ``pending_unresolved`` reads and clears it): a caller that cannot rule them out
+        takes ``sample_batch`` instead."""
         B, Vr = logits.shape
         lo, hi = shard_range(vocab_total, self.world, self.rank)
         if Vr != hi - lo:
@@ -159,16 +184,23 @@ class ShardedSampler:
         dist.all_gather_into_tensor(buf["gathered"], buf["local"], group=self.group)
         self.kernels.merge(logits, params, uniforms, history, lo, vocab_total, self.record_cap,
                            buf["gathered"], self.world, out, buf["unresolved"], probs_out)
-        # identical on every rank: all ranks take the fallback for the same rows. One boolean
-        # read per step (the count only when some row is unresolved, which is rare).
-        n = 0
-        if bool(buf["unresolved"].any()):
-            n = int(torch.count_nonzero(buf["unresolved"]))
-        self.last_unresolved = n
-        if n:
-            self._resolve(logits, params, uniforms, history, vocab_total, out, probs_out,
-                          torch.nonzero(buf["unresolved"]).flatten())
+        self._total(dev).add_(buf["unresolved"].sum())
         return out
+
+    def _total(self, device: torch.device) -> torch.Tensor:
+        t = self._totals.get(str(device))
+        if t is None:
+            t = torch.zeros((), dtype=torch.int64, device=device)
+            self._totals[str(device)] = t
+        return t
+
+    def pending_unresolved(self, device: torch.device) -> int:
+        """Rows left unresolved by ``sample_batch_async`` calls since the last read (one
+        synchronising read); then zero."""
+        t = self._total(device)
+        n = int(t.item())
+        t.zero_()
+        return n
 
     def _resolve(self, logits, params, uniforms, history, vocab_total, out, probs_out, idx):
         """Assemble the full rows ``idx`` from every rank's shard and sample them unsharded.
