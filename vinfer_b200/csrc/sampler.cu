@@ -52,6 +52,7 @@ constexpr int KC = 32;                  // candidates kept per run when top-k is
 constexpr int MAX_NSEG = 64;
 constexpr int CTA_CAP = 1024;          // resident CTAs assumed when sizing workspaces
 constexpr int MERGE_CAP = 2048;         // merged entries (input in cand, sorted in scratch)
+constexpr int DV_CAP = 1024;            // delegates whose 16 bytes are kept in shared memory
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr double FX_ONE = 17592186044416.0;      // 2^44: fixed-point unit of probability mass
 constexpr unsigned FULLMASK = 0xffffffffu;
@@ -143,7 +144,25 @@ struct __align__(16) Smem {
   uint32_t ylo_key;                    // the run's threshold: ordered key of a raw logit
   unsigned long long dkth;             // the run's K-th largest unflagged delegate
   int rhi[MAX_NSEG];                   // k_finish: end (global id) of each run of the row
+  uint4 dv[DV_CAP];                    // the first delegates' 16 bytes (or edge element)
+  float prm[8];                        // the run's row parameters (load_param order)
 };
+
+// k_stream's shared memory: the common part, then the run's staged history (ids ascending, and
+// their counts) and the run's candidates, which a CTA that streams a whole row finishes from
+constexpr int HCAP = 2048;
+struct __align__(16) SSmem {
+  Smem s;
+  int hid[HCAP];
+  int hcnt[HCAP];
+  unsigned long long rc[CAND_CAP];
+};
+
+// A row's arrival counter (workspace): runs of a row split over several CTAs add 1 each as their
+// records complete; the CTA completing the row (or the only one) then stores one of these marks.
+constexpr int CNT_READY = 0x20000000;  // the records are complete: k_finish finishes the row
+constexpr int CNT_DONE = 0x40000000;   // the streaming kernel finished the row
+static_assert(MAX_NSEG < CNT_READY, "run counts stay below the marks");
 
 // scalar slots in Smem::sc / Smem::sf
 enum { SC_NC = 0, SC_NRET, SC_TKEY, SC_LAST, SC_B, SC_J, SC_X0, SC_X1, SC_NQ, SC_RFL, SC_NH,
@@ -188,6 +207,19 @@ __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
   asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
                : "memory");
   return old;
+}
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// 4-byte asynchronous copy global -> shared memory (no registers held while in flight)
+__device__ __forceinline__ void cp_async4(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(sdst)),
+               "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // ---- element access ---------------------------------------------------------------------------
@@ -1708,11 +1740,14 @@ __device__ __forceinline__ bool hist_any(const RunHist& h, int id0, int n) {
   return (two & mask) != 0ull;
 }
 
-// Note one delegate in the run's list (any lane). Returns its slot; slots past the list are
-// counted, not written (the run then takes the exact search).
-__device__ __forceinline__ int dele_push(Smem& S, unsigned long long d) {
+// Note one delegate in the run's list (any lane), with its data (the 16-byte vector, or the edge
+// element in .x) for the first DV_CAP, so the run's end expands them without reading them again.
+// Returns its slot; slots past the list are counted, not written (the run then takes the exact
+// search).
+__device__ __forceinline__ int dele_push(Smem& S, unsigned long long d, const uint4& q) {
   const int pos = atomicAdd(&S.sc[SC_NC], 1);
   if (pos < CAND_BUF) S.cand[pos] = d;
+  if (pos < DV_CAP) S.dv[pos] = q;
   return pos;
 }
 
@@ -1773,6 +1808,21 @@ struct SegLoad {
   int nvec;       // vectors in the segment
 };
 
+// One 16-byte streaming load: read once, so it allocates no L1 line and is the first to go from
+// L2 (the kernels' code, parameters, histories and records stay cached while logits stream by).
+__device__ __forceinline__ uint4 ld_stream(const uint4* p, uint64_t pol) {
+  uint4 r;
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p), "l"(pol));
+  return r;
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 template <typename TIn>
 __device__ __forceinline__ void load_segment(const KParams& P, const TIn* rowp, int seg,
                                              SegLoad<TIn>& L) {
@@ -1790,10 +1840,11 @@ __device__ __forceinline__ void load_segment(const KParams& P, const TIn* rowp, 
   const uint4* vb = reinterpret_cast<const uint4*>(rowp + lo + head);
   L.vb = vb;
   L.gid0 = P.voff + lo + head;
+  const uint64_t pol = evict_first_policy();
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const int j = tid + NT * u;
-    L.q[u] = j < L.nvec ? __ldg(vb + j) : make_uint4(0u, 0u, 0u, 0u);
+    L.q[u] = j < L.nvec ? ld_stream(vb + j, pol) : make_uint4(0u, 0u, 0u, 0u);
   }
   L.sid = -1;
   L.sy = -INFINITY;
@@ -2114,6 +2165,118 @@ __device__ __forceinline__ void warp_first_bound(const KParams& P, const SegLoad
 }
 
 // ---------------------------------------------------------------------------------------------
+// finishing a row inside the streaming kernel
+// ---------------------------------------------------------------------------------------------
+// The CTA that completes a row (or streams all of it) finishes the row itself when its
+// candidates decide it: every kind of row except rows without top-k, whose softmax sum needs the
+// penalised terms k_finish stages. Same decisions as k_finish: the K largest candidates with the
+// ties of the K-th, the check that the K-th reaches every run's threshold (maxkey; all_in when
+// no run raised one), then the cut and the draw (mode 0) or this rank's shard record (mode 1).
+// cand[0, nc) are the row's candidates in shared memory, unsorted (nc <= CAND_BUF); the row's
+// parameters are in Smem::prm. Called by the whole CTA; returns false (the same on every
+// thread) when k_finish must finish the row.
+__device__ __noinline__ bool fast_finish(const KParams& P, Smem& S, int row,
+                                         unsigned long long* cand, int nc, uint32_t maxkey,
+                                         bool all_in) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  float prm[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) prm[i] = S.prm[i];
+  const RowCfg c = cfg_from(P, prm);
+  const bool local = P.mode == 1;
+  RecHdr* oh = local ? reinterpret_cast<RecHdr*>(P.shard_out + (size_t)row * P.shard_stride)
+                     : nullptr;
+  unsigned long long* oe = reinterpret_cast<unsigned long long*>(oh + 1);
+  const int K = c.greedy ? 1 : c.K;
+  if (c.greedy && !c.pen) {
+    // one entry per run: the smallest composite key is the first index of the maximum
+    if (tid == 0) {
+      unsigned long long b = ~0ull;
+      for (int i = 0; i < nc; ++i) b = cand[i] < b ? cand[i] : b;
+      const int nret = b != ~0ull;
+      if (local) {
+        const uint32_t rfl = (nret && P.V > 1) ? REC_UNRETAINED : 0u;
+        if (nret) oe[0] = b;
+        oh->m_y = -INFINITY;
+        oh->s = 0.f;
+        oh->n = nret;
+        oh->t_key = rfl ? comp_key(b) : 0u;
+        oh->flags = rfl;
+      } else if (nret) {
+        write_state(P, row, 2, comp_id(b), 0.f, 0.f, 0u, 0);
+      } else {
+        write_state(P, row, 3, -1, 0.f, 0.f, 0u, 0);
+        status_or(P, VINFER_ST_NONFINITE);
+      }
+    }
+    return true;
+  }
+  int nret;
+  uint32_t tkey;
+  if (nc <= 32) {  // one warp sorts the short list
+    if (w == 0) {
+      unsigned long long x = lane < nc ? cand[lane] : ~0ull;
+      x = warp_sort32(x);
+      cand[lane] = x;
+      const unsigned long long kx = __shfl_sync(FULLMASK, x, min(K, 32) - 1);
+      const uint32_t tk = nc >= K ? comp_key(kx) : 0u;
+      const int nr =
+          nc >= K ? __popc(__ballot_sync(FULLMASK, lane < nc && comp_key(x) >= tk)) : nc;
+      if (lane == 0) {
+        S.sc[SC_NRET] = nr;
+        S.sc[SC_TKEY] = (int)tk;
+      }
+    }
+    cbar();
+    nret = S.sc[SC_NRET];
+    tkey = (uint32_t)S.sc[SC_TKEY];
+  } else {
+    nret = select_inplace(cand, nc, K, &tkey, S);
+  }
+  // every element at or above each run's threshold is a candidate; the top-K cut is known only
+  // when the K-th candidate reaches all of them
+  const bool cut_ok = all_in || (nc >= K && tkey >= maxkey);
+  if (!cut_ok) return false;
+  const bool more = !(all_in && nret == nc);
+  const uint32_t dkey = max(nc >= K ? tkey : 0u, maxkey);
+  const uint32_t rflags = more ? REC_UNRETAINED : 0u;
+  if (local) {  // this rank's shard record: the sorted entries and the completeness key
+    if (nret > P.shard_cap) {
+      if (tid == 0) write_flag_hdr(oh, REC_OVERFLOW, -INFINITY, 0.f);
+      return true;
+    }
+    for (int j = tid; j < nret; j += NT) oe[j] = cand[j];
+    if (tid == 0) {
+      oh->m_y = -INFINITY;
+      oh->s = 0.f;
+      oh->n = nret;
+      oh->t_key = rflags ? dkey : 0u;
+      oh->flags = rflags;
+    }
+    return true;
+  }
+  MergeIn mi;
+  mi.m_y = -INFINITY;
+  mi.s = 0.f;
+  mi.d_key = dkey;
+  mi.flags = rflags;
+  mi.n = nret;
+  bool done;
+  if (nret >= 1 && nret <= 64 && !c.greedy) {  // one warp, no CTA barriers
+    if (w == 0) {
+      const bool d = finalize_warp(P, c, row, mi, cand);
+      if (lane == 0) S.sc[SC_X1] = d;
+    }
+    cbar();
+    done = S.sc[SC_X1] != 0;
+  } else {
+    done = finalize_sorted(P, c, row, mi, cand, S);
+  }
+  cbar();
+  return done;
+}
+
+// ---------------------------------------------------------------------------------------------
 // k_stream: every row streamed once; each run leaves an unsorted candidate record
 // ---------------------------------------------------------------------------------------------
 // A run record (global workspace, one slot per row and run): the run's threshold on raw logits,
@@ -2198,12 +2361,13 @@ __device__ __forceinline__ void stream_run(const KParams& P, Smem& S, int row, i
     for (int u = 0; u < U; ++u) {
       if (tid + NT * u < L.nvec && vm[u] >= ylo) {  // rare
         const int id0 = (int)(L.gid0 + (int64_t)(tid + NT * u) * A);
-        const int pos = dele_push(S, dele(vm[u], (uint32_t)id0));
+        const int pos = dele_push(S, dele(vm[u], (uint32_t)id0), L.q[u]);
         if (pos % TB == TB - 1 && pos < CAND_BUF) trig = pos - (TB - 1);
       }
     }
     if (L.sid >= 0 && L.sy >= ylo) {
-      const int pos = dele_push(S, dele(L.sy, DL_ONE | (uint32_t)L.sid));
+      const int pos = dele_push(S, dele(L.sy, DL_ONE | (uint32_t)L.sid),
+                                make_uint4(__float_as_uint(L.sy), 0u, 0u, 0u));
       if (pos % TB == TB - 1 && pos < CAND_BUF) trig = pos - (TB - 1);
     }
     unsigned tb = __ballot_sync(FULLMASK, trig >= 0);
@@ -2223,17 +2387,41 @@ __device__ __forceinline__ void stream_run(const KParams& P, Smem& S, int row, i
   }
 }
 
-// One run: segments seg_a..seg_b of `row`, streamed by the whole CTA, leaving its record.
+// The row's history count of `id` among the staged entries (ascending ids); 0 when absent.
+__device__ __forceinline__ int staged_count(const SSmem& X, int nh, int id) {
+  int a = 0, b = nh;
+  while (a < b) {
+    const int mid = (a + b) >> 1;
+    if (X.hid[mid] < id) a = mid + 1; else b = mid;
+  }
+  return (a < nh && X.hid[a] == id) ? X.hcnt[a] : 0;
+}
+
+// One run: segments seg_a..seg_b of `row`, streamed by the whole CTA. Its candidates end in
+// shared memory (SSmem::rc). The CTA that completes the row (or streams all of it) finishes the
+// row when the candidates decide it; otherwise the records go to the workspace and the row is
+// marked ready for k_finish.
 template <typename TIn>
-__device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_a, int seg_b) {
+__device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg_a, int seg_b) {
+  Smem& S = X.s;
   const int tid = threadIdx.x;
+  // the row's history span loads with its parameters (one round trip)
+  const int64_t ia = P.hrow ? __ldg(P.hrow + row) : 0;
+  const int64_t ib = P.hrow ? __ldg(P.hrow + row + 1) : 0;
   // the loop keeps only these scalars of the row's configuration
-  bool greedy, pen, need_sum, active;
+  bool greedy, pen, need_sum, active, mono;
   float T, c2;
   int K;
   uint32_t flags;
   {
-    const RowCfg c = load_row(P, row);
+    float prm[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) prm[i] = load_param(P, row, i);
+    if (tid == 0) {  // kept for the run's end (no global round trip there)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) S.prm[i] = prm[i];
+    }
+    const RowCfg c = cfg_from(P, prm);
     greedy = c.greedy;
     pen = c.pen;
     need_sum = c.need_sum;
@@ -2242,42 +2430,54 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
     T = c.T;
     c2 = c.c2;
     K = c.greedy ? 1 : c.K;
+    // penalties that never raise a logit: a penalised token reaches the threshold only if its
+    // raw logit does, so the delegates hold it
+    mono = c.rep >= 1.f && c.pres >= 0.f && c.freq >= 0.f;
   }
   const bool cands = !greedy || pen;  // greedy with penalties runs as top-1 candidates
-  const int run_idx = blockIdx.x - seg_owner(P, row * P.nseg);
-  unsigned char* rec = P.recs + ((size_t)row * P.nseg + run_idx) * REC_STRIDE;
-  RunRec* hd = reinterpret_cast<RunRec*>(rec);
-  unsigned long long* ent = reinterpret_cast<unsigned long long*>(rec + sizeof(RunRec));
-  // the first segment's loads go out before the set-up below, which they overlap
+  const int nh = (pen && active) ? (int)(ib - ia) : 0;
+  const bool staged = pen && active && nh <= HCAP;
+  // the history entries go out first, ahead of the segment's loads, straight to shared memory
+  if (staged) {
+    for (int j = tid; j < nh; j += NT) {
+      cp_async4(&X.hid[j], P.hids + ia + j);
+      cp_async4(&X.hcnt[j], P.hcnt + ia + j);
+    }
+  }
   SegLoad<TIn> first;
   if (active) load_segment<TIn>(P, (const TIn*)P.logits + (int64_t)row * P.ld, seg_a, first);
-  // ---- the history entries inside this run's ids, staged in shared memory
+  // ---- a bitmap of the row's penalised ids of this shard (lookups: one shared-memory load)
   if (tid == 0) S.sc[SC_NH] = 0;
   if (pen && active) {
-    // a bitmap of the row's penalised ids of this shard (lookups: one shared-memory load)
     uint32_t* bm = reinterpret_cast<uint32_t*>(S.scratch);
     const int words = (int)((P.V + 31) / 32);
     for (int i = tid; i < words; i += NT) bm[i] = 0u;
-    const int64_t ia = __ldg(P.hrow + row);
-    const int nh = (int)(__ldg(P.hrow + row + 1) - ia);
     if (tid == 0) {  // for the penalised candidates at the end of the run
       S.hpos = ia;
       S.sc[SC_NH] = nh;
     }
+    if (staged) cp_async_wait_all();
     cbar();
-    constexpr int PB = 8;  // entries per thread fetched together
-    for (int j0 = 0; j0 < nh; j0 += PB * NT) {
-      int id[PB], cn[PB];
-#pragma unroll
-      for (int k = 0; k < PB; ++k) {
-        const int j = j0 + k * NT + tid;
-        id[k] = j < nh ? __ldg(P.hids + ia + j) : 0;
-        cn[k] = j < nh ? __ldg(P.hcnt + ia + j) : 0;
+    if (staged) {
+      for (int j = tid; j < nh; j += NT) {
+        const int64_t li = (int64_t)X.hid[j] - P.voff;
+        if (X.hcnt[j] > 0 && li >= 0 && li < P.V) atomicOr(&bm[li >> 5], 1u << (li & 31));
       }
+    } else {
+      constexpr int PB = 8;  // entries per thread fetched together
+      for (int j0 = 0; j0 < nh; j0 += PB * NT) {
+        int id[PB], cn[PB];
 #pragma unroll
-      for (int k = 0; k < PB; ++k) {
-        const int64_t li = (int64_t)id[k] - P.voff;
-        if (cn[k] > 0 && li >= 0 && li < P.V) atomicOr(&bm[li >> 5], 1u << (li & 31));
+        for (int k = 0; k < PB; ++k) {
+          const int j = j0 + k * NT + tid;
+          id[k] = j < nh ? __ldg(P.hids + ia + j) : 0;
+          cn[k] = j < nh ? __ldg(P.hcnt + ia + j) : 0;
+        }
+#pragma unroll
+        for (int k = 0; k < PB; ++k) {
+          const int64_t li = (int64_t)id[k] - P.voff;
+          if (cn[k] > 0 && li >= 0 && li < P.V) atomicOr(&bm[li >> 5], 1u << (li & 31));
+        }
       }
     }
   }
@@ -2294,158 +2494,244 @@ __device__ __forceinline__ void run(const KParams& P, Smem& S, int row, int seg_
   float m_t = -FLT_MAX, s_t = 0.f;
   unsigned long long gbest = ~0ull;
   cbar();
-  if (!active) {
-    if (tid == 0) {
-      hd->m = -INFINITY;
-      hd->s = 0.f;
-      hd->ylo_key = 0u;
-      hd->n = 0;
-      hd->flags = flags;
-      __threadfence();
-      atom_add_acq_rel(&P.counters[row], 1);
-    }
-    return;
-  }
-  if (!cands)
-    stream_run<TIn, MODE_GREEDY>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first, m_t,
-                                 s_t, gbest);
-  else if (need_sum)
-    stream_run<TIn, MODE_CANDS_SUM>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first,
-                                    m_t, s_t, gbest);
-  else if (K > 32)
-    stream_run<TIn, MODE_CANDS, true>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first, m_t,
-                                      s_t, gbest);
-  else
-    stream_run<TIn, MODE_CANDS>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first, m_t, s_t,
-                                gbest);
-  cbar();
-  // ---- the record: the delegates (unsorted), the threshold, the sum of rows without top-k
   float m = -INFINITY, sum = 0.f;
-  if (need_sum) {
-    const uint32_t mk = cta_max_u32(okey(m_t == -FLT_MAX ? -INFINITY : m_t), S);
-    m = from_okey(mk);
-    const float part = (m_t == -FLT_MAX) ? 0.f : s_t * ex2((m_t - m) * c2);
-    cta_excl_scan_f(part, &sum, S);
-  }
   int n = 0;
-  if (!cands) {
-    const unsigned long long b = cta_min_u64(gbest, S);
-    if (b != ~0ull) {
-      if (tid == 0) ent[0] = b;
-      n = 1;
+  if (active) {
+    if (!cands)
+      stream_run<TIn, MODE_GREEDY>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first, m_t,
+                                   s_t, gbest);
+    else if (need_sum)
+      stream_run<TIn, MODE_CANDS_SUM>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first,
+                                      m_t, s_t, gbest);
+    else if (K > 32)
+      stream_run<TIn, MODE_CANDS, true>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first,
+                                        m_t, s_t, gbest);
+    else
+      stream_run<TIn, MODE_CANDS>(P, S, row, seg_a, seg_b, K, T, c2, greedy, pen, first, m_t,
+                                  s_t, gbest);
+    cbar();
+    // ---- the run's candidates: the delegates, the threshold, the sum of rows without top-k
+    if (need_sum) {
+      const uint32_t mk = cta_max_u32(okey(m_t == -FLT_MAX ? -INFINITY : m_t), S);
+      m = from_okey(mk);
+      const float part = (m_t == -FLT_MAX) ? 0.f : s_t * ex2((m_t - m) * c2);
+      cta_excl_scan_f(part, &sum, S);
     }
-  } else if (S.sc[SC_NC] > CAND_BUF) {
-    flags |= REC_OVERFLOW;  // ties of the threshold flooded the list: exact search
-  } else {
-    // the delegates at or above the final threshold are read again (just streamed, so from
-    // cache) and every non-penalised element at or above it is a candidate; then the penalised
-    // tokens of top-k rows with their exact values
-    using E = Elem<TIn>;
-    const float ylo = from_okey(S.ylo_key);
-    const int nd = S.sc[SC_NC];
-    const TIn* rowp = (const TIn*)P.logits + (int64_t)row * P.ld;
-    const RunHist h = hist_view(P, S);
-    RowCfg cq{};
-    cq.T = T;
-    cq.greedy = greedy;
-    auto emit = [&](float y, int id) {
-      if (!(y >= ylo)) return;
-      if (pen && hist_count(h, id) > 0) return;
-      const int pos = atomicAdd(&S.sc[SC_NRET], 1);
-      if (pos < CAND_CAP) ent[pos] = comp(okey(vf(y, cq)), id);
-    };
-    constexpr int DB = 2;  // delegate vectors per thread in flight
-    for (int i0 = 0; i0 < nd; i0 += DB * NT) {
-      uint4 q[DB];
-      uint32_t xb[DB];
-#pragma unroll
-      for (int k = 0; k < DB; ++k) {
-        const int i = i0 + k * NT + tid;
-        const unsigned long long x = i < nd ? S.cand[i] : ~0ull;
-        xb[k] = (i < nd && dele_max(x) >= ylo) ? (uint32_t)x : ~0u;
-        q[k] = make_uint4(0u, 0u, 0u, 0u);
-        if (xb[k] != ~0u) {
-          const int64_t li = (int64_t)(xb[k] & DL_ID) - P.voff;
-          if (xb[k] & DL_ONE) q[k].x = __float_as_uint(E::ld(rowp, li));
-          else q[k] = __ldg(reinterpret_cast<const uint4*>(rowp + li));
-        }
+    if (!cands) {
+      const unsigned long long b = cta_min_u64(gbest, S);
+      if (b != ~0ull) {
+        if (tid == 0) X.rc[0] = b;
+        n = 1;
       }
-#pragma unroll
-      for (int k = 0; k < DB; ++k) {
-        if (xb[k] == ~0u) continue;
-        const int id0 = (int)(xb[k] & DL_ID);
-        if (xb[k] & DL_ONE) {
-          emit(__uint_as_float(q[k].x), id0);
-        } else {
-#pragma unroll
-          for (int e = 0; e < E::A; ++e) emit(E::at(q[k], e), id0 + e);
-        }
-      }
-    }
-    if (pen && !need_sum) {
-      // the penalised tokens of this run's ids at or above the threshold, with their exact
-      // values (their logits were just streamed, so from cache). Rows without top-k leave them
-      // to the finishing kernel, which also corrects the softmax sum with them.
+    } else if (S.sc[SC_NC] > CAND_BUF) {
+      flags |= REC_OVERFLOW;  // ties of the threshold flooded the list: exact search
+    } else {
+      // the delegates at or above the final threshold are expanded (their 16 bytes were kept
+      // in shared memory; past DV_CAP they are read again, from cache) and every element at or
+      // above it is a candidate. Penalised elements: with penalties that never raise a logit,
+      // their exact values here (count from the staged history); otherwise top-k rows gather
+      // all their penalised tokens below, and rows without top-k leave them to k_finish, which
+      // also corrects the softmax sum with them.
+      using E = Elem<TIn>;
+      const float ylo = from_okey(S.ylo_key);
+      const int nd = S.sc[SC_NC];
+      const TIn* rowp = (const TIn*)P.logits + (int64_t)row * P.ld;
+      const RunHist h = hist_view(P, S);
+      RowCfg cq{};
+      cq.T = T;
+      cq.greedy = greedy;
+      const bool pen_here = pen && !need_sum && mono && staged;
       RowCfg cp{};  // what penalize() needs
-      cp.rep = load_param(P, row, 3);
-      cp.pres = load_param(P, row, 4);
-      cp.freq = load_param(P, row, 5);
-      const int64_t ia = S.hpos;
-      const int nh = S.sc[SC_NH];
-      const int64_t idlo = P.voff + (int64_t)seg_a * P.seg_len;
-      const int64_t idhi = P.voff + min(P.V, (int64_t)(seg_b + 1) * P.seg_len);
-      constexpr int PB = 8;  // entries per thread fetched together
-      for (int j0 = 0; j0 < nh; j0 += PB * NT) {
-        int id[PB], cn[PB];
-        float raw[PB];
+      cp.rep = S.prm[3];
+      cp.pres = S.prm[4];
+      cp.freq = S.prm[5];
+      auto emit = [&](float y, int id) {
+        if (!(y >= ylo)) return;
+        if (pen && hist_count(h, id) > 0) {
+          if (!pen_here) return;
+          y = penalize(y, staged_count(X, nh, id), cp);
+          if (!(y >= ylo)) return;
+        }
+        const int pos = atomicAdd(&S.sc[SC_NRET], 1);
+        if (pos < CAND_CAP) X.rc[pos] = comp(okey(vf(y, cq)), id);
+      };
+      constexpr int DB = 2;  // delegate vectors per thread in flight
+      for (int i0 = 0; i0 < nd; i0 += DB * NT) {
+        uint4 q[DB];
+        uint32_t xb[DB];
 #pragma unroll
-        for (int k = 0; k < PB; ++k) {
-          const int j = j0 + k * NT + tid;
-          id[k] = j < nh ? __ldg(P.hids + ia + j) : 0;
-          cn[k] = j < nh ? __ldg(P.hcnt + ia + j) : 0;
+        for (int k = 0; k < DB; ++k) {
+          const int i = i0 + k * NT + tid;
+          const unsigned long long x = i < nd ? S.cand[i] : ~0ull;
+          xb[k] = (i < nd && dele_max(x) >= ylo) ? (uint32_t)x : ~0u;
+          q[k] = make_uint4(0u, 0u, 0u, 0u);
+          if (xb[k] != ~0u) {
+            const int64_t li = (int64_t)(xb[k] & DL_ID) - P.voff;
+            if (i < DV_CAP) q[k] = S.dv[i];
+            else if (xb[k] & DL_ONE) q[k].x = __float_as_uint(E::ld(rowp, li));
+            else q[k] = __ldg(reinterpret_cast<const uint4*>(rowp + li));
+          }
         }
 #pragma unroll
-        for (int k = 0; k < PB; ++k) {
-          if (id[k] < idlo || id[k] >= idhi) cn[k] = 0;  // another run's, or outside the shard
-          raw[k] = cn[k] > 0 ? E::ld(rowp, (int64_t)id[k] - P.voff) : 0.f;
-        }
+        for (int k = 0; k < DB; ++k) {
+          if (xb[k] == ~0u) continue;
+          const int id0 = (int)(xb[k] & DL_ID);
+          if (xb[k] & DL_ONE) {
+            emit(__uint_as_float(q[k].x), id0);
+          } else {
 #pragma unroll
-        for (int k = 0; k < PB; ++k) {
-          if (cn[k] <= 0) continue;
-          const float yt = penalize(raw[k], cn[k], cp);
-          if (yt >= ylo) {
-            const int pos = atomicAdd(&S.sc[SC_NRET], 1);
-            if (pos < CAND_CAP) ent[pos] = comp(okey(vf(yt, cq)), id[k]);
+            for (int e = 0; e < E::A; ++e) emit(E::at(q[k], e), id0 + e);
           }
         }
       }
-    }
-    cbar();
-    n = S.sc[SC_NRET];
-    if (n > CAND_CAP) {
-      flags |= REC_OVERFLOW;
-      n = 0;
+      if (pen && !need_sum && !pen_here) {
+        // the penalised tokens of this run's ids at or above the threshold, with their exact
+        // values (their logits were just streamed, so from cache)
+        const int64_t idlo = P.voff + (int64_t)seg_a * P.seg_len;
+        const int64_t idhi = P.voff + min(P.V, (int64_t)(seg_b + 1) * P.seg_len);
+        constexpr int PB = 8;  // entries per thread fetched together
+        for (int j0 = 0; j0 < nh; j0 += PB * NT) {
+          int id[PB], cn[PB];
+          float raw[PB];
+#pragma unroll
+          for (int k = 0; k < PB; ++k) {
+            const int j = j0 + k * NT + tid;
+            id[k] = j < nh ? (staged ? X.hid[j] : __ldg(P.hids + ia + j)) : 0;
+            cn[k] = j < nh ? (staged ? X.hcnt[j] : __ldg(P.hcnt + ia + j)) : 0;
+          }
+#pragma unroll
+          for (int k = 0; k < PB; ++k) {
+            if (id[k] < idlo || id[k] >= idhi) cn[k] = 0;  // another run's, or outside the shard
+            raw[k] = cn[k] > 0 ? E::ld(rowp, (int64_t)id[k] - P.voff) : 0.f;
+          }
+#pragma unroll
+          for (int k = 0; k < PB; ++k) {
+            if (cn[k] <= 0) continue;
+            const float yt = penalize(raw[k], cn[k], cp);
+            if (yt >= ylo) {
+              const int pos = atomicAdd(&S.sc[SC_NRET], 1);
+              if (pos < CAND_CAP) X.rc[pos] = comp(okey(vf(yt, cq)), id[k]);
+            }
+          }
+        }
+      }
+      cbar();
+      n = S.sc[SC_NRET];
+      if (n > CAND_CAP) {
+        flags |= REC_OVERFLOW;
+        n = 0;
+      }
     }
   }
-  // the record is complete: count it for the row (k_finish may be waiting on exactly this).
-  // The barrier orders every thread's entries before thread 0's fence, whose release
-  // covers them.
+  cbar();
+  // ---- publish: finish the row here, or leave the record for the CTA completing the row / k_finish
+  const uint32_t ylo_key = S.ylo_key;
+  const int r0 = seg_owner(P, row * P.nseg);
+  const int nruns = seg_owner(P, row * P.nseg + P.nseg - 1) - r0 + 1;
+  unsigned char* base = P.recs + (size_t)row * P.nseg * REC_STRIDE;
+  unsigned char* rec = base + (size_t)(blockIdx.x - r0) * REC_STRIDE;
+  RunRec* hd = reinterpret_cast<RunRec*>(rec);
+  unsigned long long* ent = reinterpret_cast<unsigned long long*>(rec + sizeof(RunRec));
+  RowCfg cq{};
+  cq.T = T;
+  cq.greedy = greedy;
+  auto write_record = [&]() {
+    for (int j = tid; j < n; j += NT) ent[j] = X.rc[j];
+    if (tid == 0) {
+      hd->m = m;
+      hd->s = sum;
+      hd->ylo_key = ylo_key;
+      hd->n = n;
+      hd->flags = flags;
+    }
+  };
+  bool done = false;
+  if (nruns == 1) {  // this CTA streamed the whole row
+    if (flags == 0 && !need_sum) {
+      const float y = from_okey(ylo_key);
+      const bool all_in = !(y > -INFINITY);
+      done = fast_finish(P, S, row, X.rc, n, all_in ? 0u : okey(vf(y, cq)), all_in);
+    }
+    if (!done) write_record();
+    // the barrier orders every thread's writes before thread 0's fence, whose release covers
+    // them. A finished row needs no fence: k_finish reads nothing of it, and waits for this grid
+    // to complete before it exits itself.
+    cbar();
+    if (tid == 0) {
+      if (done) {
+        *reinterpret_cast<volatile int*>(P.counters + row) = CNT_DONE;
+      } else {
+        __threadfence();
+        st_release(P.counters + row, CNT_READY);
+      }
+    }
+    return;
+  }
+  write_record();
   cbar();
   if (tid == 0) {
-    hd->m = m;
-    hd->s = sum;
-    hd->ylo_key = S.ylo_key;
-    hd->n = n;
-    hd->flags = flags;
     __threadfence();
-    atom_add_acq_rel(&P.counters[row], 1);
+    S.sc[SC_LAST] = atom_add_acq_rel(P.counters + row, 1) == nruns - 1;
+  }
+  cbar();
+  if (!S.sc[SC_LAST]) return;
+  // the CTA completing the row: every run's header, then (when they allow it) their candidates
+  RunRec* rh = reinterpret_cast<RunRec*>(S.mh);
+  if (tid < nruns) {
+    const RunRec* src = reinterpret_cast<const RunRec*>(base + (size_t)tid * REC_STRIDE);
+    RunRec r;
+    r.ylo_key = __ldcg(&src->ylo_key);
+    r.n = __ldcg(&src->n);
+    r.flags = __ldcg(&src->flags);
+    rh[tid] = r;
+  }
+  cbar();
+  if (tid == 0) {
+    uint32_t fl = 0, maxkey = 0;
+    int tot = 0, all_in = 1;
+    for (int r = 0; r < nruns; ++r) {
+      fl |= rh[r].flags;
+      S.moff[r] = tot;
+      tot += rh[r].n;
+      const float y = from_okey(rh[r].ylo_key);
+      if (y > -INFINITY) {
+        all_in = 0;
+        maxkey = max(maxkey, okey(vf(y, cq)));
+      }
+    }
+    S.moff[nruns] = tot;
+    S.sc[SC_X0] = (fl == 0 && !need_sum && tot <= CAND_BUF) ? tot : -1;
+    S.sc[SC_J] = (int)maxkey;
+    S.sc[SC_B] = all_in;
+  }
+  cbar();
+  const int tot = S.sc[SC_X0];
+  if (tot >= 0) {
+    for (int idx = tid; idx < tot; idx += NT) {
+      int r = 0;
+      while (S.moff[r + 1] <= idx) ++r;
+      const unsigned long long* re = reinterpret_cast<const unsigned long long*>(
+          base + (size_t)r * REC_STRIDE + sizeof(RunRec));
+      S.cand[idx] = __ldcg(re + (idx - S.moff[r]));
+    }
+    cbar();
+    done = fast_finish(P, S, row, S.cand, tot, (uint32_t)S.sc[SC_J], S.sc[SC_B] != 0);
+  }
+  cbar();
+  if (tid == 0) {
+    if (done) {
+      *reinterpret_cast<volatile int*>(P.counters + row) = CNT_DONE;
+    } else {
+      __threadfence();
+      st_release(P.counters + row, CNT_READY);
+    }
   }
 }
 
 template <typename TIn>
 __global__ void __launch_bounds__(NT, 2) k_stream(const __grid_constant__ KParams P) {
   extern __shared__ __align__(128) unsigned char smraw[];
-  Smem& S = *reinterpret_cast<Smem*>(smraw);
+  SSmem& X = *reinterpret_cast<SSmem*>(smraw);
   // k_finish may be scheduled as soon as SMs free up; it waits for this grid's records itself
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int s0 = seg_begin(P, blockIdx.x), s1 = seg_begin(P, blockIdx.x + 1);
@@ -2454,7 +2740,7 @@ __global__ void __launch_bounds__(NT, 2) k_stream(const __grid_constant__ KParam
     const int row = sg / P.nseg;
     const int seg_a = sg - row * P.nseg;
     const int seg_b = min(s1 - row * P.nseg, P.nseg) - 1;
-    run<TIn>(P, S, row, seg_a, seg_b);
+    run<TIn>(P, X, row, seg_a, seg_b);
     cbar();
     sg = row * P.nseg + seg_b + 1;
   }
@@ -2466,11 +2752,10 @@ __global__ void __launch_bounds__(NT, 2) k_stream(const __grid_constant__ KParam
 // row
 // ---------------------------------------------------------------------------------------------
 
+// A row the streaming kernel left ready (its records are complete): the whole CTA.
 template <typename TIn>
-__global__ void __launch_bounds__(NT, 3) k_finish(const __grid_constant__ KParams P) {
+__device__ __forceinline__ void finish_ready(const KParams& P, Smem& S) {
   using E = Elem<TIn>;
-  extern __shared__ __align__(128) unsigned char smraw[];
-  Smem& S = *reinterpret_cast<Smem*>(smraw);
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int row = blockIdx.x;
   const RowCfg c = load_row(P, row);
@@ -2512,7 +2797,7 @@ __global__ void __launch_bounds__(NT, 3) k_finish(const __grid_constant__ KParam
   const int K = c.greedy ? 1 : c.K;
   const int nh = S.sc[SC_NH];
   const bool hshared = nh <= FCAP;
-  // ---- the penalised values of the history entries: inputs only, so before the wait
+  // ---- the penalised values of the history entries
   if (hist_here && hshared) {
     constexpr int PB = 8;  // entries per thread whose ids and logits are fetched together
     for (int j0 = 0; j0 < nh; j0 += PB * NT) {
@@ -2540,19 +2825,6 @@ __global__ void __launch_bounds__(NT, 3) k_finish(const __grid_constant__ KParam
       }
     }
   }
-  // everything above reads inputs only; the run records come from k_stream. The row is ready
-  // once all its runs have counted their records; a bounded wait for that, and should it run
-  // out, the wait for the whole streaming grid (which always ends).
-  if (tid == 0) {
-    int ready = 0;
-    for (int it = 0; it < 20000 && !ready; ++it) {
-      ready = ld_acquire(P.counters + row) >= nruns;
-      if (!ready) __nanosleep(128);
-    }
-    S.sc[SC_LAST] = ready;
-  }
-  cbar();
-  if (!S.sc[SC_LAST]) asm volatile("griddepcontrol.wait;" ::: "memory");
   if (tid < nruns) {
     const RunRec* src = reinterpret_cast<const RunRec*>(base + (size_t)tid * REC_STRIDE);
     RunRec r;
@@ -2759,6 +3031,40 @@ __global__ void __launch_bounds__(NT, 3) k_finish(const __grid_constant__ KParam
   if (!done) exact_row<TIn>(P, c, row, S, reinterpret_cast<unsigned char*>(S.scratch));
 }
 
+// One CTA per row. The row's counter carries a mark once the streaming kernel is through with
+// the row (CNT_DONE: finished there; CNT_READY: records complete); a bounded wait for it first,
+// and should it run out, the wait for the whole streaming grid (which always ends). Every CTA
+// also waits for the streaming grid before it exits, so this grid completes after it: work
+// queued behind the sampler may read every row's outputs.
+template <typename TIn>
+__global__ void __launch_bounds__(NT, 3) k_finish(const __grid_constant__ KParams P) {
+  extern __shared__ __align__(128) unsigned char smraw[];
+  Smem& S = *reinterpret_cast<Smem*>(smraw);
+  const int tid = threadIdx.x, row = blockIdx.x;
+  if (tid == 0) {
+    int v = 0;
+    for (int it = 0; it < 20000; ++it) {
+      v = ld_acquire(P.counters + row);
+      if (v >= CNT_READY) break;
+      __nanosleep(128);
+    }
+    S.sc[SC_LAST] = v;
+  }
+  cbar();
+  if (S.sc[SC_LAST] < CNT_READY) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    cbar();
+    if (tid == 0) S.sc[SC_LAST] = ld_acquire(P.counters + row);
+    cbar();
+  }
+  if (S.sc[SC_LAST] & CNT_DONE) {
+    if (tid == 0) P.counters[row] = 0;  // ready for the next call (stream-ordered after this one)
+  } else {
+    finish_ready<TIn>(P, S);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // kernels: sharded merge and probabilities
 // ---------------------------------------------------------------------------------------------
@@ -2949,7 +3255,7 @@ int kernel_info(const void* kern, int slot, int threads, size_t smem, int* ctas)
 int sample_ctas(int dtype, int* ctas) {
   const void* kern = dtype == VINFER_DTYPE_BF16 ? (const void*)k_stream<__nv_bfloat16>
                                                 : (const void*)k_stream<float>;
-  if (kernel_info(kern, dtype == VINFER_DTYPE_BF16 ? 0 : 1, NT, sizeof(Smem), ctas) != VINFER_OK)
+  if (kernel_info(kern, dtype == VINFER_DTYPE_BF16 ? 0 : 1, NT, sizeof(SSmem), ctas) != VINFER_OK)
     return VINFER_E_CUDA;
   *ctas = std::min(*ctas, CTA_CAP);
   return VINFER_OK;
@@ -2960,8 +3266,8 @@ int launch_sample(const KParams& P, int dtype, cudaStream_t st) {
   const void* fin = bf ? (const void*)k_finish<__nv_bfloat16> : (const void*)k_finish<float>;
   int unused = 0;
   if (kernel_info(fin, bf ? 4 : 5, NT, sizeof(Smem), &unused) != VINFER_OK) return VINFER_E_CUDA;
-  if (bf) k_stream<__nv_bfloat16><<<P.grid, NT, sizeof(Smem), st>>>(P);
-  else k_stream<float><<<P.grid, NT, sizeof(Smem), st>>>(P);
+  if (bf) k_stream<__nv_bfloat16><<<P.grid, NT, sizeof(SSmem), st>>>(P);
+  else k_stream<float><<<P.grid, NT, sizeof(SSmem), st>>>(P);
   if (cudaGetLastError() != cudaSuccess) return VINFER_E_CUDA;
   // programmatic dependent launch: k_finish starts on SMs as k_stream frees them and does its
   // input-only set-up before waiting for k_stream's records
