@@ -1777,23 +1777,26 @@ __device__ __forceinline__ void block_tighten(const KParams& P, int b0, int K, f
     if (v1 != ~0ull && hist_any(h, (int)((uint32_t)v1 & DL_ID), ((uint32_t)v1 & DL_ONE) ? 1 : vec_len))
       v1 = ~0ull;
   }
-  int r0 = 0, r1 = 0;
+  // the K-th largest ordered key of the block's counted delegates (absent ones have key 0): a
+  // radix select, most significant bit first, one pair of ballots per bit
+  const int nv = __popc(__ballot_sync(FULLMASK, v0 != ~0ull)) +
+                 __popc(__ballot_sync(FULLMASK, v1 != ~0ull));
+  if (nv < K) return;
+  const uint32_t ka = ~(uint32_t)(v0 >> 32), kb = ~(uint32_t)(v1 >> 32);
+  uint32_t prefix = 0u;
+  int need = K;
 #pragma unroll 4
-  for (int k = 0; k < 32; ++k) {
-    const unsigned long long a = __shfl_sync(FULLMASK, v0, k), b = __shfl_sync(FULLMASK, v1, k);
-    r0 += (a < v0) + (b < v0);
-    r1 += (a < v1) + (b < v1);
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t hi = ~((1u << bit) - 1u), cand = prefix | (1u << bit);
+    const int n = __popc(__ballot_sync(FULLMASK, (ka & hi) == cand)) +
+                  __popc(__ballot_sync(FULLMASK, (kb & hi) == cand));
+    if (n >= need) prefix = cand;
+    else need -= n;
   }
-  unsigned long long kth = ~0ull;
-  if (v0 != ~0ull && r0 == K - 1) kth = v0;
-  if (v1 != ~0ull && r1 == K - 1) kth = v1;
-  const unsigned have = __ballot_sync(FULLMASK, kth != ~0ull);
-  if (!have) return;
-  kth = __shfl_sync(FULLMASK, kth, __ffs(have) - 1);
   RowCfg c{};
   c.T = T;
   c.greedy = greedy;
-  const float y = ylo_for(vf(dele_max(kth), c), c);
+  const float y = ylo_for(vf(from_okey(prefix), c), c);
   if (lane == 0) atomicMax(&S.ylo_key, okey(y));
 }
 
@@ -2211,6 +2214,58 @@ __device__ __noinline__ bool fast_finish(const KParams& P, Smem& S, int row,
     }
     return true;
   }
+  if (nc <= 64 && !c.greedy) {  // short lists: one warp sorts, selects, cuts and draws
+    if (w == 0) {
+      unsigned long long a = lane < nc ? cand[lane] : ~0ull;
+      unsigned long long b = lane + 32 < nc ? cand[lane + 32] : ~0ull;
+      warp_sort64(a, b);
+      cand[lane] = a;
+      cand[lane + 32] = b;
+      __syncwarp();
+      uint32_t tk = 0u;
+      if (nc >= K) tk = comp_key(__shfl_sync(FULLMASK, K - 1 < 32 ? a : b, (K - 1) & 31));
+      const int nr = nc >= K ? __popc(__ballot_sync(FULLMASK, lane < nc && comp_key(a) >= tk)) +
+                                   __popc(__ballot_sync(FULLMASK, lane + 32 < nc && comp_key(b) >= tk))
+                             : nc;
+      int res = 0;
+      if (all_in || (nc >= K && tk >= maxkey)) {  // the top-K cut is known
+        const bool more = !(all_in && nr == nc);
+        const uint32_t dkey = max(nc >= K ? tk : 0u, maxkey);
+        const uint32_t rflags = more ? REC_UNRETAINED : 0u;
+        res = 1;
+        if (local) {
+          if (nr > P.shard_cap) {
+            if (lane == 0) write_flag_hdr(oh, REC_OVERFLOW, -INFINITY, 0.f);
+          } else {
+            for (int j = lane; j < nr; j += 32) oe[j] = cand[j];
+            if (lane == 0) {
+              oh->m_y = -INFINITY;
+              oh->s = 0.f;
+              oh->n = nr;
+              oh->t_key = rflags ? dkey : 0u;
+              oh->flags = rflags;
+            }
+          }
+        } else if (nr == 0) {
+          if (lane == 0) {
+            write_state(P, row, 3, -1, 0.f, 0.f, 0u, 0);
+            status_or(P, VINFER_ST_NONFINITE);
+          }
+        } else {
+          MergeIn mi;
+          mi.m_y = -INFINITY;
+          mi.s = 0.f;
+          mi.d_key = dkey;
+          mi.flags = rflags;
+          mi.n = nr;
+          res = finalize_warp(P, c, row, mi, cand) ? 1 : 0;
+        }
+      }
+      if (lane == 0) S.sc[SC_X1] = res;
+    }
+    cbar();
+    return S.sc[SC_X1] != 0;
+  }
   int nret;
   uint32_t tkey;
   if (nc <= 32) {  // one warp sorts the short list
@@ -2520,7 +2575,7 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
     if (!cands) {
       const unsigned long long b = cta_min_u64(gbest, S);
       if (b != ~0ull) {
-        if (tid == 0) X.rc[0] = b;
+        if (tid == 0) S.cand[0] = b;
         n = 1;
       }
     } else if (S.sc[SC_NC] > CAND_BUF) {
@@ -2545,43 +2600,64 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
       cp.rep = S.prm[3];
       cp.pres = S.prm[4];
       cp.freq = S.prm[5];
-      auto emit = [&](float y, int id) {
-        if (!(y >= ylo)) return;
-        if (pen && hist_count(h, id) > 0) {
-          if (!pen_here) return;
-          y = penalize(y, staged_count(X, nh, id), cp);
-          if (!(y >= ylo)) return;
+      // (1) every element of the delegates at or above the threshold whose raw logit reaches it,
+      //     as (raw bits, id) in SSmem::rc
+      if (tid == 0) S.sc[SC_X1] = 0;
+      cbar();
+      for (int i = tid; i < nd; i += NT) {
+        const unsigned long long x = S.cand[i];
+        if (!(dele_max(x) >= ylo)) continue;
+        const uint32_t xb = (uint32_t)x;
+        const int id0 = (int)(xb & DL_ID);
+        uint4 q;
+        if (i < DV_CAP) {
+          q = S.dv[i];
+        } else {
+          const int64_t li = (int64_t)id0 - P.voff;
+          if (xb & DL_ONE) q = make_uint4(__float_as_uint(E::ld(rowp, li)), 0u, 0u, 0u);
+          else q = __ldg(reinterpret_cast<const uint4*>(rowp + li));
         }
-        const int pos = atomicAdd(&S.sc[SC_NRET], 1);
-        if (pos < CAND_CAP) X.rc[pos] = comp(okey(vf(y, cq)), id);
-      };
-      constexpr int DB = 2;  // delegate vectors per thread in flight
-      for (int i0 = 0; i0 < nd; i0 += DB * NT) {
-        uint4 q[DB];
-        uint32_t xb[DB];
-#pragma unroll
-        for (int k = 0; k < DB; ++k) {
-          const int i = i0 + k * NT + tid;
-          const unsigned long long x = i < nd ? S.cand[i] : ~0ull;
-          xb[k] = (i < nd && dele_max(x) >= ylo) ? (uint32_t)x : ~0u;
-          q[k] = make_uint4(0u, 0u, 0u, 0u);
-          if (xb[k] != ~0u) {
-            const int64_t li = (int64_t)(xb[k] & DL_ID) - P.voff;
-            if (i < DV_CAP) q[k] = S.dv[i];
-            else if (xb[k] & DL_ONE) q[k].x = __float_as_uint(E::ld(rowp, li));
-            else q[k] = __ldg(reinterpret_cast<const uint4*>(rowp + li));
+        const int ne = (xb & DL_ONE) ? 1 : E::A;
+#pragma unroll 1
+        for (int e = 0; e < ne; ++e) {
+          const float y = (xb & DL_ONE) ? __uint_as_float(q.x) : E::at(q, e);
+          if (y >= ylo) {
+            const int pos = atomicAdd(&S.sc[SC_X1], 1);
+            if (pos < CAND_CAP)
+              X.rc[pos] = ((unsigned long long)__float_as_uint(y) << 32) | (uint32_t)(id0 + e);
           }
         }
-#pragma unroll
-        for (int k = 0; k < DB; ++k) {
-          if (xb[k] == ~0u) continue;
-          const int id0 = (int)(xb[k] & DL_ID);
-          if (xb[k] & DL_ONE) {
-            emit(__uint_as_float(q[k].x), id0);
-          } else {
-#pragma unroll
-            for (int e = 0; e < E::A; ++e) emit(E::at(q[k], e), id0 + e);
+      }
+      cbar();
+      // (2) one element per thread: penalties, the processed value, the candidate entry; the
+      //     delegate list is spent, so the candidates go to Smem::cand (warp-aggregated slots)
+      const int nq = S.sc[SC_X1];
+      if (nq > CAND_CAP) {
+        flags |= REC_OVERFLOW;
+      } else {
+        for (int j0 = 0; j0 < nq; j0 += NT) {
+          const int j = j0 + tid;
+          bool keep = false;
+          unsigned long long ce = 0ull;
+          if (j < nq) {
+            const unsigned long long r = X.rc[j];
+            float y = __uint_as_float((uint32_t)(r >> 32));
+            const int id = (int)(uint32_t)r;
+            keep = true;
+            if (pen && hist_count(h, id) > 0) {
+              keep = pen_here;  // otherwise gathered below (or, without top-k, by k_finish)
+              if (keep) {
+                y = penalize(y, staged_count(X, nh, id), cp);
+                keep = y >= ylo;
+              }
+            }
+            if (keep) ce = comp(okey(vf(y, cq)), id);
           }
+          const unsigned bal = __ballot_sync(FULLMASK, keep);
+          int base = 0;
+          if ((tid & 31) == 0 && bal) base = atomicAdd(&S.sc[SC_NRET], __popc(bal));
+          base = __shfl_sync(FULLMASK, base, 0);
+          if (keep) S.cand[base + __popc(bal & ((1u << (tid & 31)) - 1u))] = ce;
         }
       }
       if (pen && !need_sum && !pen_here) {
@@ -2610,7 +2686,7 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
             const float yt = penalize(raw[k], cn[k], cp);
             if (yt >= ylo) {
               const int pos = atomicAdd(&S.sc[SC_NRET], 1);
-              if (pos < CAND_CAP) X.rc[pos] = comp(okey(vf(yt, cq)), id[k]);
+              if (pos < CAND_BUF) S.cand[pos] = comp(okey(vf(yt, cq)), id[k]);
             }
           }
         }
@@ -2636,7 +2712,7 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
   cq.T = T;
   cq.greedy = greedy;
   auto write_record = [&]() {
-    for (int j = tid; j < n; j += NT) ent[j] = X.rc[j];
+    for (int j = tid; j < n; j += NT) ent[j] = S.cand[j];
     if (tid == 0) {
       hd->m = m;
       hd->s = sum;
@@ -2650,7 +2726,7 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
     if (flags == 0 && !need_sum) {
       const float y = from_okey(ylo_key);
       const bool all_in = !(y > -INFINITY);
-      done = fast_finish(P, S, row, X.rc, n, all_in ? 0u : okey(vf(y, cq)), all_in);
+      done = fast_finish(P, S, row, S.cand, n, all_in ? 0u : okey(vf(y, cq)), all_in);
     }
     if (!done) write_record();
     // the barrier orders every thread's writes before thread 0's fence, whose release covers
