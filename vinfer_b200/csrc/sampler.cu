@@ -124,6 +124,12 @@ struct KParams {
   size_t shard_stride;
 };
 
+struct RowCfg {
+  float T, c2, p, minp, lm, rep, pres, freq, u;
+  int k, K;
+  bool greedy, topk, need_sum, pen, bad, exact;
+};
+
 struct __align__(16) Smem {
   unsigned long long cand[CAND_BUF];   // run candidates (composite keys), sorted in place;
                                        // merge input; exact search: row bitmap words
@@ -146,6 +152,7 @@ struct __align__(16) Smem {
   int rhi[MAX_NSEG];                   // k_finish: end (global id) of each run of the row
   uint4 dv[DV_CAP];                    // the first delegates' 16 bytes (or edge element)
   float prm[8];                        // the run's row parameters (load_param order)
+  RowCfg cfg;                          // ... and the configuration made from them
 };
 
 // k_stream's shared memory: the common part, then the run's staged history (ids ascending, and
@@ -304,11 +311,6 @@ struct Elem<__nv_bfloat16> {
 // ---------------------------------------------------------------------------------------------
 // per-row configuration
 // ---------------------------------------------------------------------------------------------
-struct RowCfg {
-  float T, c2, p, minp, lm, rep, pres, freq, u;
-  int k, K;
-  bool greedy, topk, need_sum, pen, bad, exact;
-};
 
 __device__ RowCfg make_cfg(const KParams& P, float T, int k, float p, float minp, float rep,
                            float pres, float freq, float u) {
@@ -2182,10 +2184,7 @@ __device__ __noinline__ bool fast_finish(const KParams& P, Smem& S, int row,
                                          unsigned long long* cand, int nc, uint32_t maxkey,
                                          bool all_in) {
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  float prm[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) prm[i] = S.prm[i];
-  const RowCfg c = cfg_from(P, prm);
+  const RowCfg c = S.cfg;  // made at the run's set-up
   const bool local = P.mode == 1;
   RecHdr* oh = local ? reinterpret_cast<RecHdr*>(P.shard_out + (size_t)row * P.shard_stride)
                      : nullptr;
@@ -2216,9 +2215,23 @@ __device__ __noinline__ bool fast_finish(const KParams& P, Smem& S, int row,
   }
   if (nc <= 64 && !c.greedy) {  // short lists: one warp sorts, selects, cuts and draws
     if (w == 0) {
+      // sorted by counting ranks (entries are distinct): independent shared-memory reads
+      // instead of a chain of shuffle stages
       unsigned long long a = lane < nc ? cand[lane] : ~0ull;
       unsigned long long b = lane + 32 < nc ? cand[lane + 32] : ~0ull;
-      warp_sort64(a, b);
+      int ra = 0, rb = 0;
+#pragma unroll 8
+      for (int j = 0; j < nc; ++j) {
+        const unsigned long long x = cand[j];
+        ra += x < a;
+        rb += x < b;
+      }
+      unsigned long long* srt = S.scratch;  // free once the run's candidates are made
+      if (lane < nc) srt[ra] = a;
+      if (lane + 32 < nc) srt[rb] = b;
+      __syncwarp();
+      a = lane < nc ? srt[lane] : ~0ull;
+      b = lane + 32 < nc ? srt[lane + 32] : ~0ull;
       cand[lane] = a;
       cand[lane + 32] = b;
       __syncwarp();
@@ -2443,13 +2456,13 @@ __device__ __forceinline__ void stream_run(const KParams& P, Smem& S, int row, i
 }
 
 // The row's history count of `id` among the staged entries (ascending ids); 0 when absent.
-__device__ __forceinline__ int staged_count(const SSmem& X, int nh, int id) {
+__device__ __forceinline__ int staged_count(const int* hid, const int* hcnt, int nh, int id) {
   int a = 0, b = nh;
   while (a < b) {
     const int mid = (a + b) >> 1;
-    if (X.hid[mid] < id) a = mid + 1; else b = mid;
+    if (hid[mid] < id) a = mid + 1; else b = mid;
   }
-  return (a < nh && X.hid[a] == id) ? X.hcnt[a] : 0;
+  return (a < nh && hid[a] == id) ? hcnt[a] : 0;
 }
 
 // One run: segments seg_a..seg_b of `row`, streamed by the whole CTA. Its candidates end in
@@ -2477,6 +2490,7 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
       for (int i = 0; i < 8; ++i) S.prm[i] = prm[i];
     }
     const RowCfg c = cfg_from(P, prm);
+    if (tid == 0) S.cfg = c;
     greedy = c.greedy;
     pen = c.pen;
     need_sum = c.need_sum;
@@ -2493,6 +2507,8 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
   const int nh = (pen && active) ? (int)(ib - ia) : 0;
   const bool staged = pen && active && nh <= HCAP;
   // the history entries go out first, ahead of the segment's loads, straight to shared memory
+  const int* hid = X.hid;
+  const int* hcnt = X.hcnt;
   if (staged) {
     for (int j = tid; j < nh; j += NT) {
       cp_async4(&X.hid[j], P.hids + ia + j);
@@ -2515,8 +2531,8 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
     cbar();
     if (staged) {
       for (int j = tid; j < nh; j += NT) {
-        const int64_t li = (int64_t)X.hid[j] - P.voff;
-        if (X.hcnt[j] > 0 && li >= 0 && li < P.V) atomicOr(&bm[li >> 5], 1u << (li & 31));
+        const int64_t li = (int64_t)hid[j] - P.voff;
+        if (hcnt[j] > 0 && li >= 0 && li < P.V) atomicOr(&bm[li >> 5], 1u << (li & 31));
       }
     } else {
       constexpr int PB = 8;  // entries per thread fetched together
@@ -2647,7 +2663,7 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
             if (pen && hist_count(h, id) > 0) {
               keep = pen_here;  // otherwise gathered below (or, without top-k, by k_finish)
               if (keep) {
-                y = penalize(y, staged_count(X, nh, id), cp);
+                y = penalize(y, staged_count(hid, hcnt, nh, id), cp);
                 keep = y >= ylo;
               }
             }
@@ -2672,8 +2688,8 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
 #pragma unroll
           for (int k = 0; k < PB; ++k) {
             const int j = j0 + k * NT + tid;
-            id[k] = j < nh ? (staged ? X.hid[j] : __ldg(P.hids + ia + j)) : 0;
-            cn[k] = j < nh ? (staged ? X.hcnt[j] : __ldg(P.hcnt + ia + j)) : 0;
+            id[k] = j < nh ? (staged ? hid[j] : __ldg(P.hids + ia + j)) : 0;
+            cn[k] = j < nh ? (staged ? hcnt[j] : __ldg(P.hcnt + ia + j)) : 0;
           }
 #pragma unroll
           for (int k = 0; k < PB; ++k) {
