@@ -243,6 +243,17 @@ def bench_single(args) -> dict:
     clk = clocks.stop()
     backend.check()
 
+    # the other single-GPU configurations, timed the same way (outside the headline's timed
+    # region): 2 (the reference's default request shape among its rows), 5 (adversarial rows,
+    # top-k up to 1,000) and 4 unsharded (the reference point of the vocab-sharded lines)
+    other_configs = {}
+    if not topp:
+        for n, k_n in ((2, min(K, 400)), (5, min(K, 20))):
+            other_configs[str(n)] = config_rows_per_s(n, dev, k_n)
+        c4_rows = unsharded_config4_rows_per_s(backend_c4(dev), dev, min(K, 200))
+        other_configs["4_unsharded"] = {"rows_per_s": c4_rows, "ms_per_step": 1024 / c4_rows * 1e3,
+                                        "batch": 1024, "vocab": 248_320, "dtype": "bf16"}
+
     # end to end through the public API: host inputs in, ids out, every step
     e2e_steps = max(3, min(K, 20))
     host_logits = w.logits.pin_memory()
@@ -321,6 +332,7 @@ def bench_single(args) -> dict:
                 "d2h_bytes_per_step": B * 4, "steps": e2e_steps},
         "gpu_launches": 2 * K,  # k_stream and k_finish per step
         "cpu_baseline": cpu,
+        "configs": other_configs,
     }
 
 
@@ -457,6 +469,55 @@ def graphed(step, K: int):
         graphs.append(g)
     torch.cuda.synchronize()
     return graphs, [graphs[0]] * (K // G) + ([graphs[1]] if K % G else []), G
+
+
+def config_rows_per_s(n: int, dev, K: int) -> dict:
+    """Configuration ``n`` (2 or 5) on this GPU through ``sample_batch`` in CUDA graphs, with
+    rotating logits buffers (more than 2x L2 in total): rows/s and the device time per batch."""
+    from vinfer_b200 import SAMPLER, BackendContext  # noqa: PLC0415
+    from vinfer_b200.sampling import RowParams, TokenHistogram  # noqa: PLC0415
+    from vinfer_b200.workloads import make  # noqa: PLC0415
+
+    w = make(n)
+    B = w.batch
+    backend = SAMPLER.resolve("b200", BackendContext(dev, w.logits.dtype))
+    base = w.logits.to(dev)
+    nb = base.numel() * base.element_size()
+    nbuf = max(2, int(np.ceil(2 * L2_BYTES / nb)) + 1)
+    bufs = [base] + [base.clone() for _ in range(nbuf - 1)]
+    params = RowParams.from_arrays(dev, **w.param_arrays())
+    u = torch.from_numpy(w.uniforms).to(dev)
+    hist = (TokenHistogram.from_csr(w.hist_row_ptr, w.hist_ids, w.hist_counts, dev)
+            if w.hist_row_ptr is not None else None)
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+
+    def step(i: int) -> None:
+        backend.sample_batch(bufs[i % nbuf], params, u, hist, out=out)
+
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize()
+    backend.check()
+    graphs, plan, _ = graphed(step, K)
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for g in plan:
+        g.replay()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    backend.check()
+    ms = t0.elapsed_time(t1) / K
+    del graphs, plan, bufs
+    return {"rows_per_s": B / (ms * 1e-3), "ms_per_step": ms, "batch": B, "vocab": w.vocab,
+            "dtype": "bf16" if w.logits.dtype == torch.bfloat16 else "f32", "steps": K,
+            "l2": f"{nbuf} rotating logits buffers"}
+
+
+def backend_c4(dev):
+    from vinfer_b200 import SAMPLER, BackendContext  # noqa: PLC0415
+
+    return SAMPLER.resolve("b200", BackendContext(dev, torch.bfloat16))
 
 
 def unsharded_config4_rows_per_s(backend, dev, K: int) -> float:
