@@ -53,6 +53,7 @@ extern "C" {
 /* bits OR-ed into *status by the device */
 #define VINFER_ST_BAD_PARAM 1u   /* a row's parameters are invalid; its id is -1 */
 #define VINFER_ST_NONFINITE 2u   /* a row has no finite maximum after processing */
+#define VINFER_ST_HIST_FULL 4u   /* vinfer_hist_append: a slot had no room for a new token */
 #define VINFER_ST_INTERNAL 8u    /* an internal consistency check failed */
 
 /* args.flags */
@@ -140,6 +141,32 @@ int vinfer_sample_merge(const VinferSampleArgs* args, int32_t record_cap, const 
  */
 #define VINFER_STATIC_SCRATCH_BYTES (32u << 20)
 int vinfer_sample_static(const VinferSampleArgs* args, void* stream);
+
+/* ---- slotted histories for a batched decode loop ----------------------------------------------
+ * Replaces the host-side loop of src/vinfer/runtime/generate.py:127-143 (one sample() per step,
+ * an int() host sync per token, no token counts kept) for a batch of decode slots, each owned
+ * by one request as in src/vinfer/state/pool.py:70-82 (alloc / free of per-request state).
+ * Slot s owns entries [s * cap, (s + 1) * cap) of hist_ids / hist_counts (int32): its first
+ * hist_len[s] entries are its tokens (ids strictly ascending, counts > 0); the others are
+ * padding with count 0 and id VINFER_HIST_PAD_ID - (cap - 1 - position), ascending and above
+ * every vocabulary id. With row_ptr[s] = s * cap (int64 [slots + 1]) the arrays are a CSR
+ * history that vinfer_sample reads as it is (padding entries are outside every vocabulary),
+ * so sample -> append -> sample never leaves the device.
+ *  - vinfer_hist_append: for every slot s with tokens[s] >= 0, count tokens[s] once more in
+ *    slot s, or insert it in id order. A full slot (hist_len[s] == cap) keeps its counts and
+ *    sets VINFER_ST_HIST_FULL in *status (may be NULL). tokens is typically the previous
+ *    vinfer_sample's out_ids (an invalid row's id -1 changes nothing).
+ *  - vinfer_hist_reset: empty the n slots listed in slot_list (a request leaving its slot);
+ *    entries outside [0, slots) are skipped.
+ * Both are stream-ordered, one CTA per slot, and allocate nothing. cap <= VINFER_HIST_MAX_CAP.
+ */
+#define VINFER_HIST_PAD_ID 0x7FFFFFFF
+#define VINFER_HIST_MAX_CAP (1 << 20)
+int vinfer_hist_append(const int32_t* tokens, int64_t slots, int32_t* hist_ids,
+                       int32_t* hist_counts, int32_t* hist_len, int32_t cap, int32_t* status,
+                       void* stream);
+int vinfer_hist_reset(const int32_t* slot_list, int64_t n, int64_t slots, int32_t* hist_ids,
+                      int32_t* hist_counts, int32_t* hist_len, int32_t cap, void* stream);
 
 #ifdef __cplusplus
 }

@@ -358,3 +358,35 @@ def test_large_top_k_with_penalised_top_tokens(backend, k, batch, V):
     ids, probs = run_b200(backend, w)
     rep = compare(w, ids, probs)
     assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_top_k_rows_with_penalties_that_raise_logits(backend, dtype):
+    # repetition < 1 (or a negative presence / frequency penalty) lifts a penalised token, so
+    # one whose raw logit was below the run's threshold can enter the top-k: these rows take the
+    # gather of every penalised token at the run's end rather than the delegate expansion
+    V = 40_000
+    g = torch.Generator().manual_seed(21)
+    kinds = [dict(temperature=0.8, top_k=20, top_p=0.9, repetition_penalty=0.7),
+             dict(temperature=1.0, top_k=10, presence_penalty=-2.0),
+             dict(temperature=0.6, top_k=32, top_p=0.8, frequency_penalty=-0.5),
+             dict(temperature=1.0, top_k=5, repetition_penalty=0.8, presence_penalty=-1.0,
+                  frequency_penalty=0.1)]
+    params = kinds * 4
+    B = len(params)
+    x = (torch.randn(B, V, generator=g) * 2.0).to(dtype)
+    rng = np.random.default_rng(5)
+    ptr, ids_, cnt = [0], [], []
+    for r in range(B):
+        # tokens just below the top: penalties that raise them reorder the top-k
+        order = torch.argsort(x[r].float(), descending=True).numpy()
+        toks = np.concatenate([order[30:90], rng.integers(0, V, 100)])
+        u, c = np.unique(toks, return_counts=True)
+        ids_.append(u.astype(np.int32))
+        cnt.append(c.astype(np.int32))
+        ptr.append(ptr[-1] + len(u))
+    w = _workload(x, params, hist=(np.array(ptr), np.concatenate(ids_), np.concatenate(cnt)))
+    ids, probs = run_b200(backend, w)
+    rep = compare(w, ids, probs)
+    report(f"top-k rows with logit-raising penalties ({dtype})", rep)
+    assert not rep.failures, (str(rep), rep.failures[:5])

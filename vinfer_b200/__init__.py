@@ -11,6 +11,7 @@ from vinfer_b200.registry import BackendContext, BackendRegistry
 from vinfer_b200.sampling import (
     RowParams,
     SamplingParams,
+    SlotHistogram,
     TokenHistogram,
     position_seed,
     position_uniform,
@@ -24,6 +25,7 @@ __all__ = [
     "RowParams",
     "SamplerBackend",
     "SamplingParams",
+    "SlotHistogram",
     "TokenHistogram",
     "position_seed",
     "position_uniform",

@@ -17,11 +17,13 @@ ABI_VERSION = 1
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 OK, E_ARG, E_LIMIT, E_CUDA = 0, 1, 2, 3
-ST_BAD_PARAM, ST_NONFINITE, ST_INTERNAL = 1, 2, 8
+ST_BAD_PARAM, ST_NONFINITE, ST_HIST_FULL, ST_INTERNAL = 1, 2, 4, 8
 FLAG_EXACT_ALL = 1
 MAX_VOCAB = 262144
 MAX_BATCH = 65535
 STATIC_SCRATCH_BYTES = 32 << 20
+HIST_PAD_ID = 0x7FFFFFFF
+HIST_MAX_CAP = 1 << 20
 
 EXPORTS = (
     "vinfer_sampler_abi_version",
@@ -32,6 +34,8 @@ EXPORTS = (
     "vinfer_sample_local",
     "vinfer_sample_merge",
     "vinfer_sample_static",
+    "vinfer_hist_append",
+    "vinfer_hist_reset",
 )
 
 _ERRORS = {E_ARG: "invalid argument", E_LIMIT: "limit exceeded", E_CUDA: "CUDA error"}
@@ -98,6 +102,12 @@ def load() -> C.CDLL:
                                         C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
     lib.vinfer_sample_static.restype = C.c_int
     lib.vinfer_sample_static.argtypes = [C.POINTER(SampleArgs), C.c_void_p]
+    lib.vinfer_hist_append.restype = C.c_int
+    lib.vinfer_hist_append.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p,
+                                       C.c_int32, C.c_void_p, C.c_void_p]
+    lib.vinfer_hist_reset.restype = C.c_int
+    lib.vinfer_hist_reset.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.c_int32, C.c_void_p]
     version = lib.vinfer_sampler_abi_version()
     if version != ABI_VERSION:
         raise RuntimeError(f"sampler library ABI {version}, expected {ABI_VERSION}")
@@ -116,6 +126,8 @@ def status_message(bits: int) -> str:
         names.append("invalid sampling parameters in a row")
     if bits & ST_NONFINITE:
         names.append("a row has no finite logit")
+    if bits & ST_HIST_FULL:
+        names.append("a history slot was full (a token was not counted)")
     if bits & ST_INTERNAL:
         names.append("internal consistency check failed")
     return ", ".join(names) or "ok"

@@ -3209,6 +3209,90 @@ __global__ void __launch_bounds__(256) k_probs(const __grid_constant__ KParams P
 }
 
 // ---------------------------------------------------------------------------------------------
+// slotted histories: in-place count updates between decode steps
+// ---------------------------------------------------------------------------------------------
+constexpr int HIST_NT = 256;
+
+// padding id of position p of a slot with cap entries (ascending, above every vocabulary id)
+__device__ __forceinline__ int hist_pad_id(int cap, int p) {
+  return VINFER_HIST_PAD_ID - (cap - 1 - p);
+}
+
+// One CTA per slot: tokens[s] counted once more, or inserted in id order (entries from its place
+// on move up by one, chunk by chunk from the top, so no entry is overwritten before it is read).
+__global__ void __launch_bounds__(HIST_NT) k_hist_append(const int* tokens, int* ids, int* cnts,
+                                                         int* lens, int cap, int* status) {
+  const int s = blockIdx.x, tid = threadIdx.x;
+  const int t = __ldg(tokens + s);
+  if (t < 0) return;  // no token this step (an invalid row's id is -1)
+  int* sid = ids + (int64_t)s * cap;
+  int* sc = cnts + (int64_t)s * cap;
+  const int n = min(max(lens[s], 0), cap);
+  __shared__ int pos_s, found_s;
+  if (tid < 32) {
+    // the first entry whose id is >= t: a warp-wide search, 32 probes per round (each round
+    // narrows [lo, hi] to a 33rd); the predicate sid[q] < t is monotone in q
+    int lo = 0, hi = n;
+    while (hi - lo > 32) {
+      const int step = (hi - lo + 32) / 33;
+      const int q = min(lo + (tid + 1) * step, hi) - 1;
+      const int k = __popc(__ballot_sync(FULLMASK, sid[q] < t));
+      const int nlo = min(lo + k * step, hi);
+      if (k < 32) hi = min(lo + (k + 1) * step, hi);
+      lo = nlo;
+    }
+    const int q = lo + tid;
+    const int pos = lo + __popc(__ballot_sync(FULLMASK, q < hi && sid[q] < t));
+    if (tid == 0) {
+      pos_s = pos;
+      found_s = pos < n && sid[pos] == t;
+    }
+  }
+  __syncthreads();
+  const int pos = pos_s;
+  if (found_s) {
+    if (tid == 0) sc[pos] += 1;
+    return;
+  }
+  if (n >= cap) {
+    if (tid == 0 && status) atomicOr(reinterpret_cast<unsigned int*>(status), VINFER_ST_HIST_FULL);
+    return;
+  }
+  for (int hi = n; hi > pos; hi -= HIST_NT) {  // entries [lo, hi) move to [lo + 1, hi + 1)
+    const int lo = max(pos, hi - HIST_NT);
+    const int i = lo + tid;
+    int a = 0, c = 0;
+    if (i < hi) {
+      a = sid[i];
+      c = sc[i];
+    }
+    __syncthreads();
+    if (i < hi) {
+      sid[i + 1] = a;
+      sc[i + 1] = c;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    sid[pos] = t;
+    sc[pos] = 1;
+    lens[s] = n + 1;
+  }
+}
+
+// One CTA per listed slot: every entry back to padding, the length to zero.
+__global__ void __launch_bounds__(HIST_NT) k_hist_reset(const int* slot_list, int64_t slots,
+                                                        int* ids, int* cnts, int* lens, int cap) {
+  const int s = __ldg(slot_list + blockIdx.x);
+  if (s < 0 || s >= slots) return;
+  for (int p = threadIdx.x; p < cap; p += HIST_NT) {
+    ids[(int64_t)s * cap + p] = hist_pad_id(cap, p);
+    cnts[(int64_t)s * cap + p] = 0;
+  }
+  if (threadIdx.x == 0) lens[s] = 0;
+}
+
+// ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
 struct Shape {
@@ -3478,6 +3562,29 @@ int vinfer_sample_merge(const VinferSampleArgs* a, int32_t record_cap, const voi
         P, (const unsigned char*)records, world_size, unresolved);
   if (cudaGetLastError() != cudaSuccess) return VINFER_E_CUDA;
   return launch_probs(P, a->dtype, st);
+}
+
+int vinfer_hist_append(const int32_t* tokens, int64_t slots, int32_t* hist_ids,
+                       int32_t* hist_counts, int32_t* hist_len, int32_t cap, int32_t* status,
+                       void* stream) {
+  if (!tokens || !hist_ids || !hist_counts || !hist_len || slots < 1 || cap < 1)
+    return VINFER_E_ARG;
+  if (slots > VINFER_MAX_BATCH || cap > VINFER_HIST_MAX_CAP) return VINFER_E_LIMIT;
+  k_hist_append<<<(unsigned)slots, HIST_NT, 0, (cudaStream_t)stream>>>(tokens, hist_ids,
+                                                                      hist_counts, hist_len, cap,
+                                                                      status);
+  return cudaGetLastError() == cudaSuccess ? VINFER_OK : VINFER_E_CUDA;
+}
+
+int vinfer_hist_reset(const int32_t* slot_list, int64_t n, int64_t slots, int32_t* hist_ids,
+                      int32_t* hist_counts, int32_t* hist_len, int32_t cap, void* stream) {
+  if (!slot_list || !hist_ids || !hist_counts || !hist_len || n < 1 || slots < 1 || cap < 1)
+    return VINFER_E_ARG;
+  if (n > VINFER_MAX_BATCH || slots > VINFER_MAX_BATCH || cap > VINFER_HIST_MAX_CAP)
+    return VINFER_E_LIMIT;
+  k_hist_reset<<<(unsigned)n, HIST_NT, 0, (cudaStream_t)stream>>>(slot_list, slots, hist_ids,
+                                                                 hist_counts, hist_len, cap);
+  return cudaGetLastError() == cudaSuccess ? VINFER_OK : VINFER_E_CUDA;
 }
 
 }  // extern "C"

@@ -14,7 +14,13 @@ import torch
 from vinfer_b200 import _lib
 from vinfer_b200.kernels.sampler.base import SAMPLER
 from vinfer_b200.registry import BackendContext
-from vinfer_b200.sampling import RowParams, SamplingParams, TokenHistogram, position_uniform
+from vinfer_b200.sampling import (
+    RowParams,
+    SamplingParams,
+    SlotHistogram,
+    TokenHistogram,
+    position_uniform,
+)
 
 _DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
 
@@ -131,6 +137,38 @@ class B200Sampler:
         ws = self.workspace(B, V, a.dtype)
         _lib.check(self.lib.vinfer_sample(C.byref(a), ws.data_ptr(), ws.numel(), self._stream()),
                    "vinfer_sample")
+        return out
+
+    # ---- batched decode with slotted histories ------------------------------------------------
+    def append_tokens(self, slots: SlotHistogram, tokens: torch.Tensor) -> None:
+        """Count ``tokens[s]`` once more in slot ``s`` (id order kept; a negative id is no
+        token). Stream-ordered on the current stream; a full slot sets a status bit."""
+        if tokens.shape != (slots.slots,) or tokens.dtype != torch.int32 or \
+                tokens.device != self.device or not tokens.is_contiguous():
+            raise ValueError(f"tokens must be a contiguous int32 [{slots.slots}] on {self.device}")
+        _lib.check(self.lib.vinfer_hist_append(tokens.data_ptr(), slots.slots,
+                                               slots.ids.data_ptr(), slots.counts.data_ptr(),
+                                               slots.lens.data_ptr(), slots.cap,
+                                               self.status.data_ptr(), self._stream()),
+                   "vinfer_hist_append")
+
+    def reset_slots(self, slots: SlotHistogram, which: torch.Tensor) -> None:
+        """Empty the listed slots (int32 slot numbers on the device): a request leaving."""
+        if which.dtype != torch.int32 or which.device != self.device or which.dim() != 1:
+            raise ValueError(f"which must be int32 [n] on {self.device}")
+        if which.numel() == 0:
+            return
+        _lib.check(self.lib.vinfer_hist_reset(which.contiguous().data_ptr(), which.numel(),
+                                              slots.slots, slots.ids.data_ptr(),
+                                              slots.counts.data_ptr(), slots.lens.data_ptr(),
+                                              slots.cap, self._stream()), "vinfer_hist_reset")
+
+    def decode_step(self, logits: torch.Tensor, params: RowParams, uniforms: torch.Tensor,
+                    slots: SlotHistogram, out: torch.Tensor | None = None) -> torch.Tensor:
+        """One decode step of every slot: sample with the slots' histories (penalties), then
+        count the sampled ids into them. Nothing leaves the device; the ids are in ``out``."""
+        out = self.sample_batch(logits, params, uniforms, slots.history, out=out)
+        self.append_tokens(slots, out)
         return out
 
     def sample(self, logits: torch.Tensor, params: SamplingParams, seed: int,

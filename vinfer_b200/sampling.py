@@ -158,3 +158,73 @@ class TokenHistogram:
         if len(ids) == 0:
             ids, counts = np.zeros(1, np.int32), np.zeros(1, np.int32)
         return cls(t(row_ptr), t(ids), t(np.asarray(counts, np.int32)))
+
+
+HIST_PAD_ID = 0x7FFFFFFF  # VINFER_HIST_PAD_ID
+
+
+@dataclass
+class SlotHistogram:
+    """Per-slot token counts kept on the device across decode steps (``vinfer_hist_*``).
+
+    Slot ``s`` owns entries ``[s * cap, (s + 1) * cap)`` of ``ids`` / ``counts``: its first
+    ``lens[s]`` entries are its tokens (ids strictly ascending, counts > 0), the others padding
+    (count 0, ids ascending above every vocabulary id). ``history`` is therefore a CSR
+    ``TokenHistogram`` the sampler reads as it is, and the backend's ``append_tokens`` updates
+    it in place from the ids a step sampled, without leaving the device. The slots play the
+    role of vinfer's per-request state slots (``src/vinfer/state/pool.py:70-82``).
+    """
+
+    cap: int
+    ids: torch.Tensor  # int32 [slots * cap]
+    counts: torch.Tensor  # int32 [slots * cap]
+    lens: torch.Tensor  # int32 [slots]
+    row_ptr: torch.Tensor  # int64 [slots + 1], s * cap
+
+    @property
+    def slots(self) -> int:
+        return self.lens.shape[0]
+
+    @property
+    def history(self) -> TokenHistogram:
+        return TokenHistogram(self.row_ptr, self.ids, self.counts)
+
+    @staticmethod
+    def host_layout(rows: Sequence[Sequence[int]], cap: int
+                    ) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+        """(ids, counts, lens) of the slotted layout for the given token lists, on the host."""
+        if cap < 1:
+            raise ValueError("cap must be at least 1")
+        n = len(rows)
+        pos = np.arange(cap, dtype=np.int64)
+        pad = (HIST_PAD_ID - (cap - 1 - pos)).astype(np.int32)
+        ids = np.tile(pad, n)
+        counts = np.zeros(n * cap, np.int32)
+        lens = np.zeros(n, np.int32)
+        for s, toks in enumerate(rows):
+            u, c = np.unique(np.asarray(toks, dtype=np.int64), return_counts=True)
+            if len(u) > cap:
+                raise ValueError(f"slot {s} has {len(u)} distinct tokens, more than cap {cap}")
+            if len(u) and (u[0] < 0 or u[-1] >= HIST_PAD_ID - cap):
+                raise ValueError(f"slot {s} has a token id outside the vocabulary range")
+            ids[s * cap:s * cap + len(u)] = u
+            counts[s * cap:s * cap + len(u)] = c
+            lens[s] = len(u)
+        return ids, counts, lens
+
+    @classmethod
+    def from_token_lists(cls, rows: Sequence[Sequence[int]], cap: int,
+                         device: torch.device | str) -> SlotHistogram:
+        ids, counts, lens = cls.host_layout(rows, cap)
+        t = (lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device))
+        row_ptr = np.arange(len(rows) + 1, dtype=np.int64) * cap
+        return cls(cap, t(ids), t(counts), t(lens), t(row_ptr))
+
+    def to_counts(self) -> list[dict[int, int]]:
+        """Each slot's {token: count}, read back to the host (synchronises)."""
+        ids, counts, lens = (x.cpu().numpy() for x in (self.ids, self.counts, self.lens))
+        out = []
+        for s in range(self.slots):
+            a = s * self.cap
+            out.append({int(i): int(c) for i, c in zip(ids[a:a + lens[s]], counts[a:a + lens[s]])})
+        return out
