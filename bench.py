@@ -253,6 +253,7 @@ def bench_single(args) -> dict:
         c4_rows = unsharded_config4_rows_per_s(backend_c4(dev), dev, min(K, 200))
         other_configs["4_unsharded"] = {"rows_per_s": c4_rows, "ms_per_step": 1024 / c4_rows * 1e3,
                                         "batch": 1024, "vocab": 248_320, "dtype": "bf16"}
+        other_configs["3_decode"] = decode_rows_per_s(w, dev, min(K, 300))
 
     # end to end through the public API: host inputs in, ids out, every step
     e2e_steps = max(3, min(K, 20))
@@ -512,6 +513,47 @@ def config_rows_per_s(n: int, dev, K: int) -> dict:
     return {"rows_per_s": B / (ms * 1e-3), "ms_per_step": ms, "batch": B, "vocab": w.vocab,
             "dtype": "bf16" if w.logits.dtype == torch.bfloat16 else "f32", "steps": K,
             "l2": f"{nbuf} rotating logits buffers"}
+
+
+def decode_rows_per_s(w, dev, K: int) -> dict:
+    """Configuration 3 as a decode loop: every step samples all 256 slots with their slotted
+    histories (penalties) and counts the sampled ids into them in place (vinfer_hist_append),
+    with nothing leaving the device; CUDA graphs, rotating logits buffers."""
+    from vinfer_b200 import SAMPLER, BackendContext  # noqa: PLC0415
+    from vinfer_b200.sampling import RowParams, SlotHistogram  # noqa: PLC0415
+
+    B = w.batch
+    backend = SAMPLER.resolve("b200", BackendContext(dev, torch.bfloat16))
+    base = w.logits.to(dev)
+    nbuf = max(2, int(np.ceil(2 * L2_BYTES / (base.numel() * 2))) + 1)
+    bufs = [base] + [base.clone() for _ in range(nbuf - 1)]
+    params = RowParams.from_arrays(dev, **w.param_arrays())
+    u = torch.from_numpy(w.uniforms).to(dev)
+    cap = 2048  # room for the longest history (1,646 entries) plus every step's new token
+    slots = SlotHistogram.from_csr(w.hist_row_ptr, w.hist_ids, w.hist_counts, cap, dev)
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+
+    def step(i: int) -> None:
+        backend.decode_step(bufs[i % nbuf], params, u, slots, out=out)
+
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize()
+    backend.check()
+    graphs, plan, _ = graphed(step, K)
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for g in plan:
+        g.replay()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    backend.check()
+    ms = t0.elapsed_time(t1) / K
+    del graphs, plan, bufs
+    return {"rows_per_s": B / (ms * 1e-3), "ms_per_step": ms, "batch": B, "steps": K,
+            "history": f"slotted, cap {cap} entries a slot, updated in place every step",
+            "launches_per_step": 3}
 
 
 def backend_c4(dev):

@@ -220,6 +220,25 @@ class SlotHistogram:
         row_ptr = np.arange(len(rows) + 1, dtype=np.int64) * cap
         return cls(cap, t(ids), t(counts), t(lens), t(row_ptr))
 
+    @classmethod
+    def from_csr(cls, row_ptr: np.ndarray, ids: np.ndarray, counts: np.ndarray, cap: int,
+                 device: torch.device | str) -> SlotHistogram:
+        """Slots holding the rows of a CSR history (ids ascending within a row)."""
+        row_ptr = np.asarray(row_ptr, np.int64)
+        n = len(row_ptr) - 1
+        lens = np.diff(row_ptr).astype(np.int32)
+        if n and lens.max() > cap:
+            raise ValueError(f"a row has {lens.max()} entries, more than cap {cap}")
+        pos = np.arange(cap, dtype=np.int64)
+        sid = np.tile((HIST_PAD_ID - (cap - 1 - pos)).astype(np.int32), n)
+        sc = np.zeros(n * cap, np.int32)
+        for r in range(n):
+            a, b = row_ptr[r], row_ptr[r + 1]
+            sid[r * cap:r * cap + (b - a)] = ids[a:b]
+            sc[r * cap:r * cap + (b - a)] = counts[a:b]
+        t = (lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device))
+        return cls(cap, t(sid), t(sc), t(lens), t(np.arange(n + 1, dtype=np.int64) * cap))
+
     def to_counts(self) -> list[dict[int, int]]:
         """Each slot's {token: count}, read back to the host (synchronises)."""
         ids, counts, lens = (x.cpu().numpy() for x in (self.ids, self.counts, self.lens))
