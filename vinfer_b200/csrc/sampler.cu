@@ -3133,6 +3133,9 @@ __global__ void __launch_bounds__(NT, 3) k_finish(const __grid_constant__ KParam
   extern __shared__ __align__(128) unsigned char smraw[];
   Smem& S = *reinterpret_cast<Smem*>(smraw);
   const int tid = threadIdx.x, row = blockIdx.x;
+  // a kernel launched after this one as a programmatic dependent (the decode loop's history
+  // update) may be scheduled now; it waits for this grid's completion before reading anything
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0) {
     int v = 0;
     for (int it = 0; it < 20000; ++it) {
@@ -3222,8 +3225,11 @@ __device__ __forceinline__ int hist_pad_id(int cap, int p) {
 // on move up by one, chunk by chunk from the top, so no entry is overwritten before it is read).
 __global__ void __launch_bounds__(HIST_NT) k_hist_append(const int* tokens, int* ids, int* cnts,
                                                          int* lens, int cap, int* status) {
+  // launched as a programmatic dependent of the sampler: its ids are final once the kernel
+  // before this one has completed
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int s = blockIdx.x, tid = threadIdx.x;
-  const int t = __ldg(tokens + s);
+  const int t = tokens[s];
   if (t < 0) return;  // no token this step (an invalid row's id is -1)
   int* sid = ids + (int64_t)s * cap;
   int* sc = cnts + (int64_t)s * cap;
@@ -3570,10 +3576,20 @@ int vinfer_hist_append(const int32_t* tokens, int64_t slots, int32_t* hist_ids,
   if (!tokens || !hist_ids || !hist_counts || !hist_len || slots < 1 || cap < 1)
     return VINFER_E_ARG;
   if (slots > VINFER_MAX_BATCH || cap > VINFER_HIST_MAX_CAP) return VINFER_E_LIMIT;
-  k_hist_append<<<(unsigned)slots, HIST_NT, 0, (cudaStream_t)stream>>>(tokens, hist_ids,
-                                                                      hist_counts, hist_len, cap,
-                                                                      status);
-  return cudaGetLastError() == cudaSuccess ? VINFER_OK : VINFER_E_CUDA;
+  // programmatic dependent launch: scheduled while the kernel before it finishes, it waits on
+  // the device for that kernel's completion before it reads the ids
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)slots);
+  cfg.blockDim = dim3(HIST_NT);
+  cfg.stream = (cudaStream_t)stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k_hist_append, tokens, hist_ids, hist_counts,
+                                           hist_len, cap, status);
+  return e == cudaSuccess ? VINFER_OK : VINFER_E_CUDA;
 }
 
 int vinfer_hist_reset(const int32_t* slot_list, int64_t n, int64_t slots, int32_t* hist_ids,
