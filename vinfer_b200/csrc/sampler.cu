@@ -3133,9 +3133,6 @@ __global__ void __launch_bounds__(NT, 3) k_finish(const __grid_constant__ KParam
   extern __shared__ __align__(128) unsigned char smraw[];
   Smem& S = *reinterpret_cast<Smem*>(smraw);
   const int tid = threadIdx.x, row = blockIdx.x;
-  // a kernel launched after this one as a programmatic dependent (the decode loop's history
-  // update) may be scheduled now; it waits for this grid's completion before reading anything
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid == 0) {
     int v = 0;
     for (int it = 0; it < 20000; ++it) {
