@@ -107,6 +107,15 @@ int vinfer_sampler_workspace_init(void* workspace, size_t bytes, void* stream);
 int vinfer_sample(const VinferSampleArgs* args, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/* Log-probability of each row's sampled token under the row's final distribution (after
+ * penalties, temperature, top-k / top-p / min-p and renormalisation): the `logprobs` that
+ * src/vinfer/server/protocol.py:131-132 rejects today. Call after vinfer_sample with the same
+ * args and workspace (it reads the row results that call left there), before the next call on
+ * that workspace. out_logprobs: float [batch]; greedy rows get 0 (a one-hot distribution),
+ * rows without a result (invalid parameters, no finite logit) NaN. Unsharded calls only. */
+int vinfer_sample_logprobs(const VinferSampleArgs* args, float* out_logprobs, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* ---- vocab-sharded mode -------------------------------------------------------------------
  * Each rank calls vinfer_sample_local on its shard (vocab_offset / vocab_total set), which
  * writes one fixed-size candidate record per row into `records` (this rank's slice of the

@@ -390,3 +390,32 @@ def test_top_k_rows_with_penalties_that_raise_logits(backend, dtype):
     rep = compare(w, ids, probs)
     report(f"top-k rows with logit-raising penalties ({dtype})", rep)
     assert not rep.failures, (str(rep), rep.failures[:5])
+
+
+LOGPROB_ATOL = 2e-5  # natural-log units: float32 probabilities within 1e-5 relative, plus slack
+
+
+@pytest.mark.parametrize("config,batch", [(2, 24), (3, 16), (5, 16)])
+def test_logprobs_of_the_sampled_tokens(config, batch):
+    # the sampled token's log-probability under the row's final distribution, against the
+    # oracle's final probabilities; greedy rows have a one-hot distribution (log-probability 0)
+    w = make(config, batch=batch)
+    be = SAMPLER.resolve("b200", BackendContext(torch.device("cuda", 0), w.logits.dtype))
+    lg, params, u, hist = to_device(w, be.device)
+    lp = torch.empty(w.batch, dtype=torch.float32, device=be.device)
+    ids = be.sample_batch(lg, params, u, hist, logprobs_out=lp).cpu().numpy()
+    be.check()
+    lp = lp.cpu().numpy()
+    checked = 0
+    for r in range(w.batch):
+        res = oracle_row(w, r)
+        if w.temperature[r] == 0:
+            assert lp[r] == 0.0, (r, lp[r])
+            continue
+        if int(ids[r]) != res.token:
+            assert res.boundary, (r, int(ids[r]), res.token)
+            continue
+        want = float(np.log(res.probs[res.token]))
+        assert abs(float(lp[r]) - want) <= LOGPROB_ATOL, (r, float(lp[r]), want)
+        checked += 1
+    assert checked >= w.batch // 2

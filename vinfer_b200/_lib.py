@@ -34,6 +34,7 @@ EXPORTS = (
     "vinfer_sample_local",
     "vinfer_sample_merge",
     "vinfer_sample_static",
+    "vinfer_sample_logprobs",
     "vinfer_hist_append",
     "vinfer_hist_reset",
 )
@@ -102,6 +103,9 @@ def load() -> C.CDLL:
                                         C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
     lib.vinfer_sample_static.restype = C.c_int
     lib.vinfer_sample_static.argtypes = [C.POINTER(SampleArgs), C.c_void_p]
+    lib.vinfer_sample_logprobs.restype = C.c_int
+    lib.vinfer_sample_logprobs.argtypes = [C.POINTER(SampleArgs), C.c_void_p, C.c_void_p,
+                                           C.c_size_t, C.c_void_p]
     lib.vinfer_hist_append.restype = C.c_int
     lib.vinfer_hist_append.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p,
                                        C.c_int32, C.c_void_p, C.c_void_p]

@@ -3208,6 +3208,36 @@ __global__ void __launch_bounds__(256) k_probs(const __grid_constant__ KParams P
   }
 }
 
+// log-probability of each row's sampled token under the row's final distribution (penalties,
+// temperature, top-k / top-p / min-p, renormalised), from the row state the finishing step
+// left: ln p = (v_token - m_v) - ln(s_kept), where v_token is the token's processed logit.
+// One thread per row; greedy rows give 0 (their distribution is one-hot), rows without a
+// result NaN.
+template <typename TIn>
+__global__ void __launch_bounds__(128) k_logprobs(const __grid_constant__ KParams P, float* out) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= P.B) return;
+  const RowState st = P.rows[row];
+  if (st.kind == 3 || st.token < 0) {
+    out[row] = __int_as_float(0x7fc00000);
+    return;
+  }
+  if (st.kind == 2) {
+    out[row] = 0.f;
+    return;
+  }
+  const RowCfg c = load_row(P, row);
+  const int64_t li = (int64_t)st.token - P.voff;
+  float y = Elem<TIn>::ld((const TIn*)P.logits + (int64_t)row * P.ld, li);
+  if (c.pen) {
+    const int64_t ha = __ldg(P.hrow + row), hb = __ldg(P.hrow + row + 1);
+    const int64_t q = lower_bound_ids(P.hids, ha, hb, st.token);
+    if (q < hb && __ldg(P.hids + q) == st.token && __ldg(P.hcnt + q) > 0)
+      y = penalize(y, __ldg(P.hcnt + q), c);
+  }
+  out[row] = (vf(y, c) - st.m_v) - logf(st.s_kept);
+}
+
 // ---------------------------------------------------------------------------------------------
 // slotted histories: in-place count updates between decode steps
 // ---------------------------------------------------------------------------------------------
@@ -3565,6 +3595,23 @@ int vinfer_sample_merge(const VinferSampleArgs* a, int32_t record_cap, const voi
         P, (const unsigned char*)records, world_size, unresolved);
   if (cudaGetLastError() != cudaSuccess) return VINFER_E_CUDA;
   return launch_probs(P, a->dtype, st);
+}
+
+int vinfer_sample_logprobs(const VinferSampleArgs* a, float* out_logprobs, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  int rc = check_args(a);
+  if (rc != VINFER_OK) return rc;
+  if (a->vocab_offset != 0 || a->vocab_total != a->vocab) return VINFER_E_ARG;
+  if (!workspace || !out_logprobs) return VINFER_E_ARG;
+  if (workspace_bytes < ws_layout(a->batch, a->vocab, a->dtype).total) return VINFER_E_LIMIT;
+  const Shape s = plan(a->batch, a->vocab, a->dtype, 1);
+  KParams P = make_params(a, s, workspace);
+  const unsigned grid = (unsigned)((a->batch + 127) / 128);
+  if (a->dtype == VINFER_DTYPE_BF16)
+    k_logprobs<__nv_bfloat16><<<grid, 128, 0, (cudaStream_t)stream>>>(P, out_logprobs);
+  else
+    k_logprobs<float><<<grid, 128, 0, (cudaStream_t)stream>>>(P, out_logprobs);
+  return cudaGetLastError() == cudaSuccess ? VINFER_OK : VINFER_E_CUDA;
 }
 
 int vinfer_hist_append(const int32_t* tokens, int64_t slots, int32_t* hist_ids,

@@ -129,14 +129,27 @@ class B200Sampler:
     # ---- SamplerBackend ------------------------------------------------------------------------
     def sample_batch(self, logits: torch.Tensor, params: RowParams, uniforms: torch.Tensor,
                      history: TokenHistogram | None = None, out: torch.Tensor | None = None,
-                     probs_out: torch.Tensor | None = None, exact: bool = False) -> torch.Tensor:
+                     probs_out: torch.Tensor | None = None, exact: bool = False,
+                     logprobs_out: torch.Tensor | None = None) -> torch.Tensor:
+        """Sample one id per row into ``out``. ``logprobs_out`` (float32 [B], optional)
+        receives each sampled token's log-probability under the row's final distribution
+        (0 for greedy rows, NaN for rows without a result)."""
         B, V = logits.shape
         if out is None:
             out = torch.empty(B, dtype=torch.int32, device=self.device)
+        if logprobs_out is not None and (logprobs_out.shape != (B,) or
+                                         logprobs_out.dtype != torch.float32 or
+                                         logprobs_out.device != self.device or
+                                         not logprobs_out.is_contiguous()):
+            raise ValueError(f"logprobs_out must be a contiguous float32 [{B}] on {self.device}")
         a = self.args(logits, params, uniforms, history, out, probs_out, exact)
         ws = self.workspace(B, V, a.dtype)
         _lib.check(self.lib.vinfer_sample(C.byref(a), ws.data_ptr(), ws.numel(), self._stream()),
                    "vinfer_sample")
+        if logprobs_out is not None:
+            _lib.check(self.lib.vinfer_sample_logprobs(C.byref(a), logprobs_out.data_ptr(),
+                                                       ws.data_ptr(), ws.numel(),
+                                                       self._stream()), "vinfer_sample_logprobs")
         return out
 
     # ---- batched decode with slotted histories ------------------------------------------------
