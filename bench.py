@@ -44,6 +44,17 @@ def config4_workload(world: int) -> str:
     return ("config4: batch 1024 x vocab 248320 bf16 N(0,3) + 4 spikes, vocab-sharded over "
             f"{world} GPUs, local top-k 50 records, NCCL all-gather, merge on every rank, temp 1, "
             "top-k 50, top-p 0.9")
+
+
+def workload_config(world: int, hist_nnz: int | None = None) -> dict:
+    """The ``config`` object of a line: the workload alone (what both arms measure, so the two
+    arms' objects are equal); how each arm measures it goes under ``method``."""
+    if world == 1:
+        return {"workload": CONFIG3_WORKLOAD, "batch": 256, "vocab": 151_936,
+                "hist_nnz": hist_nnz}
+    return {"workload": config4_workload(world), "batch": 1024, "vocab": 248_320}
+
+
 SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -315,11 +326,11 @@ def bench_single(args) -> dict:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded, configuration 3)",
-        "config": {"workload": CONFIG3_WORKLOAD if not topp else
-                   ("config3 logits, top-p only: batch 256 x vocab 151936 bf16, temp 0.7, "
-                    "top-k 0, top-p 0.9, no penalties (rows that need the exact search)"),
-                   "batch": B, "vocab": V, "hist_nnz": w.hist_nnz if not topp else 0,
-                   "l2": f"{nbuf} rotating logits buffers "
+        "config": workload_config(1, w.hist_nnz) if not topp else
+                  {"workload": "config3 logits, top-p only: batch 256 x vocab 151936 bf16, "
+                               "temp 0.7, top-k 0, top-p 0.9, no penalties (rows that need the "
+                               "exact search)", "batch": B, "vocab": V, "hist_nnz": 0},
+        "method": {"l2": f"{nbuf} rotating logits buffers "
                          f"({nbuf * w.logits.numel() * 2 / 2**20:.0f} MiB > 2x L2)",
                    "parallelism": "single GPU", "graph_steps": G},
         "gb_per_s": algo / (ms_step * 1e-3) / 1e9,
@@ -751,8 +762,8 @@ def bench_sharded(args) -> dict | None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded on the device, configuration 4 distribution)",
-        "config": {"workload": config4_workload(world),
-                   "batch": B, "vocab": V, "shard_vocab": hi - lo,
+        "config": workload_config(world),
+        "method": {"shard_vocab": hi - lo,
                    "record_bytes_per_row": sampler.rec_bytes,
                    "allgather_bytes_per_rank": B * sampler.rec_bytes,
                    "l2": f"{nbuf} rotating shard buffers per rank "
@@ -815,10 +826,11 @@ def bench_reference(args, world: int) -> dict:
         "vs_baseline": None,
         "dtype": "f32",
         "data": f"synthetic (seeded, configuration {config})",
-        "config": {"workload": CONFIG3_WORKLOAD if config == 3 else config4_workload(world),
-                   "rows_per_step": rows_per_step,
+        "config": workload_config(world, w.hist_nnz if config == 3 else None),
+        "method": {"rows_per_step": rows_per_step,
                    "note": "each step samples rows_per_step rows of the configuration on the CPU "
-                           "(the whole row, unsharded); the metric is rows per second"},
+                           "(the whole row, unsharded), one sample() call per row as "
+                           "generate() makes them; the metric is rows per second"},
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": res["cores"], "kind": "port",
                          "sample": res["sample"]},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0,
