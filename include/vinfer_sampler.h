@@ -116,6 +116,21 @@ int vinfer_sample(const VinferSampleArgs* args, void* workspace, size_t workspac
 int vinfer_sample_logprobs(const VinferSampleArgs* args, float* out_logprobs, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* The n most likely tokens of each row's final distribution with their log-probabilities: the
+ * `top_logprobs` that src/vinfer/server/protocol.py:131-132 rejects today. Call after
+ * vinfer_sample with the same args and workspace, before the next call on that workspace; it
+ * streams the logits once more (the n largest processed values, by the candidate path) and
+ * prices each token with the row's result that call left: out_ids / out_logprobs are
+ * [batch, n] in descending probability (ties by ascending id); a token outside the kept set
+ * gets -inf, a slot with no token id -1; a greedy row lists its token with 0 (its distribution
+ * is one-hot); a row without a result (invalid parameters) gets -1 and NaN, and a row whose top
+ * list ties flood (more than 1,024 equal values) gets -1. 1 <= n <= VINFER_TOP_LOGPROBS_MAX,
+ * n < vocab. Unsharded calls only. */
+#define VINFER_TOP_LOGPROBS_MAX 32
+int vinfer_sample_top_logprobs(const VinferSampleArgs* args, int32_t n, int32_t* out_ids,
+                               float* out_logprobs, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
 /* ---- vocab-sharded mode -------------------------------------------------------------------
  * Each rank calls vinfer_sample_local on its shard (vocab_offset / vocab_total set), which
  * writes one fixed-size candidate record per row into `records` (this rank's slice of the

@@ -419,3 +419,37 @@ def test_logprobs_of_the_sampled_tokens(config, batch):
         assert abs(float(lp[r]) - want) <= LOGPROB_ATOL, (r, float(lp[r]), want)
         checked += 1
     assert checked >= w.batch // 2
+
+
+@pytest.mark.parametrize("config,batch,n", [(2, 24, 5), (3, 16, 20), (5, 16, 8)])
+def test_top_logprobs(config, batch, n):
+    # the n most likely tokens of each row's final distribution, in descending probability
+    # (ties by ascending id), with their log-probabilities; tokens outside the kept set -inf
+    w = make(config, batch=batch)
+    be = SAMPLER.resolve("b200", BackendContext(torch.device("cuda", 0), w.logits.dtype))
+    lg, params, u, hist = to_device(w, be.device)
+    ids = be.sample_batch(lg, params, u, hist).cpu().numpy()
+    tid, tlp = be.top_logprobs(lg, params, u, hist, n)
+    be.check()
+    tid, tlp = tid.cpu().numpy(), tlp.cpu().numpy()
+    checked = 0
+    for r in range(w.batch):
+        res = oracle_row(w, r)
+        if w.temperature[r] == 0:  # one-hot: the greedy token with log-probability 0
+            assert tid[r, 0] == ids[r] and tlp[r, 0] == 0.0, (r, tid[r, :2], tlp[r, :2])
+            assert np.all(np.isneginf(tlp[r, 1:])), (r, tlp[r])
+            continue
+        if res.boundary:
+            continue
+        if tid[r, 0] == -1:  # ties flooded the list (configuration 5's tied rows)
+            continue
+        p = res.probs
+        kept = np.flatnonzero(p > 0)
+        order = kept[np.lexsort((kept, -p[kept].astype(np.float64)))]
+        m = min(n, len(order))
+        assert tid[r, :m].tolist() == order[:m].tolist(), (r, tid[r, :m], order[:m])
+        want = np.log(p[order[:m]].astype(np.float64))
+        assert np.all(np.abs(tlp[r, :m] - want) <= LOGPROB_ATOL), (r, tlp[r, :m], want)
+        assert np.all(np.isneginf(tlp[r, m:])), (r, tlp[r, m:])
+        checked += 1
+    assert checked >= w.batch // 3

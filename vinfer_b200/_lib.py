@@ -23,6 +23,7 @@ MAX_VOCAB = 262144
 MAX_BATCH = 65535
 STATIC_SCRATCH_BYTES = 32 << 20
 HIST_PAD_ID = 0x7FFFFFFF
+TOP_LOGPROBS_MAX = 32
 HIST_MAX_CAP = 1 << 20
 
 EXPORTS = (
@@ -35,6 +36,7 @@ EXPORTS = (
     "vinfer_sample_merge",
     "vinfer_sample_static",
     "vinfer_sample_logprobs",
+    "vinfer_sample_top_logprobs",
     "vinfer_hist_append",
     "vinfer_hist_reset",
 )
@@ -106,6 +108,9 @@ def load() -> C.CDLL:
     lib.vinfer_sample_logprobs.restype = C.c_int
     lib.vinfer_sample_logprobs.argtypes = [C.POINTER(SampleArgs), C.c_void_p, C.c_void_p,
                                            C.c_size_t, C.c_void_p]
+    lib.vinfer_sample_top_logprobs.restype = C.c_int
+    lib.vinfer_sample_top_logprobs.argtypes = [C.POINTER(SampleArgs), C.c_int32, C.c_void_p,
+                                               C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
     lib.vinfer_hist_append.restype = C.c_int
     lib.vinfer_hist_append.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p,
                                        C.c_int32, C.c_void_p, C.c_void_p]

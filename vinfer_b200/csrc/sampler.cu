@@ -99,7 +99,8 @@ constexpr size_t REC_STRIDE = sizeof(RecHdr) + 8 * CAND_CAP;
 struct KParams {
   const void* logits;
   int64_t ld, V, voff, vtotal;
-  int B, nseg, seg_len, mode;  // mode 0: finalize, 1: local (write shard records), 2: merge
+  int B, nseg, seg_len, mode;  // mode 0: finalize, 1: local (write shard records), 2: merge,
+                               // 3: top log-probabilities of rows a mode-0 call just sampled
   int total, grid;             // segments in the batch (B * nseg) and CTAs sharing them
   uint32_t flags;
   const float* temperature;
@@ -122,6 +123,9 @@ struct KParams {
   unsigned char* shard_out;
   int shard_cap;
   size_t shard_stride;
+  int topn;          // mode 3: entries of each row's top list
+  int* top_ids;      // mode 3: [B, topn] token ids (-1: none)
+  float* top_lp;     // mode 3: [B, topn] log-probabilities
 };
 
 struct RowCfg {
@@ -314,6 +318,12 @@ struct Elem<__nv_bfloat16> {
 
 __device__ RowCfg make_cfg(const KParams& P, float T, int k, float p, float minp, float rep,
                            float pres, float freq, float u) {
+  if (P.mode == 3) {  // the n largest processed values: top-k n, no cut, no draw
+    k = P.topn;
+    p = 1.f;
+    minp = 0.f;
+    u = 0.f;
+  }
   RowCfg c;
   c.T = T;
   c.k = k;
@@ -2169,6 +2179,33 @@ __device__ __forceinline__ void warp_first_bound(const KParams& P, const SegLoad
   __syncwarp();
 }
 
+// Mode 3: a row's top list from its sorted entries e[0, m) (the m largest processed values, in
+// canonical order), each token with its log-probability under the distribution the preceding
+// sampling call left in the row state: ln p = (v - m_v) - ln(s_kept), -inf outside the kept set
+// (a greedy row's distribution is one-hot on its token). Slots past m get id -1 and -inf; a row
+// without a sampling result gets -1 and NaN. The 32 lanes of one warp.
+__device__ void write_top(const KParams& P, int row, const unsigned long long* e, int m) {
+  const int lane = threadIdx.x & 31;
+  const RowState st = P.rows[row];
+  for (int j = lane; j < P.topn; j += 32) {
+    int id = -1;
+    float lp = -INFINITY;
+    if (st.kind == 3) {
+      lp = __int_as_float(0x7fc00000);
+    } else if (j < m) {
+      id = comp_id(e[j]);
+      const uint32_t key = comp_key(e[j]);
+      bool kept;
+      if (st.kind == 2) kept = id == st.token;
+      else if (st.kind == 1) kept = true;
+      else kept = key > st.cut_key || (key == st.cut_key && id <= st.cut_id);
+      if (kept) lp = st.kind == 2 ? 0.f : (from_okey(key) - st.m_v) - logf(st.s_kept);
+    }
+    P.top_ids[(size_t)row * P.topn + j] = id;
+    P.top_lp[(size_t)row * P.topn + j] = lp;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // finishing a row inside the streaming kernel
 // ---------------------------------------------------------------------------------------------
@@ -2192,6 +2229,19 @@ __device__ __noinline__ bool fast_finish(const KParams& P, Smem& S, int row,
   const int K = c.greedy ? 1 : c.K;
   if (c.greedy && !c.pen) {
     // one entry per run: the smallest composite key is the first index of the maximum
+    if (P.mode == 3) {
+      if (w == 0) {
+        unsigned long long b = ~0ull;
+        if (lane == 0)
+          for (int i = 0; i < nc; ++i) b = cand[i] < b ? cand[i] : b;
+        b = __shfl_sync(FULLMASK, b, 0);
+        __syncwarp();
+        if (lane == 0) cand[0] = b;
+        __syncwarp();
+        write_top(P, row, cand, b != ~0ull ? 1 : 0);
+      }
+      return true;
+    }
     if (tid == 0) {
       unsigned long long b = ~0ull;
       for (int i = 0; i < nc; ++i) b = cand[i] < b ? cand[i] : b;
@@ -2246,7 +2296,9 @@ __device__ __noinline__ bool fast_finish(const KParams& P, Smem& S, int row,
         const uint32_t dkey = max(nc >= K ? tk : 0u, maxkey);
         const uint32_t rflags = more ? REC_UNRETAINED : 0u;
         res = 1;
-        if (local) {
+        if (P.mode == 3) {
+          write_top(P, row, cand, nr);
+        } else if (local) {
           if (nr > P.shard_cap) {
             if (lane == 0) write_flag_hdr(oh, REC_OVERFLOW, -INFINITY, 0.f);
           } else {
@@ -2308,6 +2360,10 @@ __device__ __noinline__ bool fast_finish(const KParams& P, Smem& S, int row,
   const bool more = !(all_in && nret == nc);
   const uint32_t dkey = max(nc >= K ? tkey : 0u, maxkey);
   const uint32_t rflags = more ? REC_UNRETAINED : 0u;
+  if (P.mode == 3) {
+    if (w == 0) write_top(P, row, cand, nret);
+    return true;
+  }
   if (local) {  // this rank's shard record: the sorted entries and the completeness key
     if (nret > P.shard_cap) {
       if (tid == 0) write_flag_hdr(oh, REC_OVERFLOW, -INFINITY, 0.f);
@@ -2958,6 +3014,10 @@ __device__ __forceinline__ void finish_ready(const KParams& P, Smem& S) {
   const bool local = P.mode == 1;
   unsigned char* shard = local ? P.shard_out + (size_t)row * P.shard_stride : nullptr;
   if (flags & REC_BAD) {
+    if (P.mode == 3) {
+      if (w == 0) write_top(P, row, cand, 0);
+      return;
+    }
     if (tid == 0) {
       if (local) {
         write_flag_hdr(reinterpret_cast<RecHdr*>(shard), REC_BAD, m_y, s_run);
@@ -3083,6 +3143,10 @@ __device__ __forceinline__ void finish_ready(const KParams& P, Smem& S) {
     }
   }
   (void)sorted_done;
+  if (P.mode == 3) {  // rows the candidates cannot decide (ties flooding a list) report none
+    if (w == 0) write_top(P, row, cand, exact ? 0 : nret);
+    return;
+  }
   if (local) {  // this rank's shard record: the sorted entries and the completeness key
     RecHdr* oh = reinterpret_cast<RecHdr*>(shard);
     unsigned long long* oe = reinterpret_cast<unsigned long long*>(shard + sizeof(RecHdr));
@@ -3595,6 +3659,27 @@ int vinfer_sample_merge(const VinferSampleArgs* a, int32_t record_cap, const voi
         P, (const unsigned char*)records, world_size, unresolved);
   if (cudaGetLastError() != cudaSuccess) return VINFER_E_CUDA;
   return launch_probs(P, a->dtype, st);
+}
+
+int vinfer_sample_top_logprobs(const VinferSampleArgs* a, int32_t n, int32_t* out_ids,
+                               float* out_logprobs, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  int rc = check_args(a);
+  if (rc != VINFER_OK) return rc;
+  if (a->vocab_offset != 0 || a->vocab_total != a->vocab) return VINFER_E_ARG;
+  if (!workspace || !out_ids || !out_logprobs || n < 1 || (int64_t)n >= a->vocab)
+    return VINFER_E_ARG;
+  if (n > VINFER_TOP_LOGPROBS_MAX) return VINFER_E_LIMIT;
+  if (workspace_bytes < ws_layout(a->batch, a->vocab, a->dtype).total) return VINFER_E_LIMIT;
+  int ctas = 0;
+  if (sample_ctas(a->dtype, &ctas) != VINFER_OK) return VINFER_E_CUDA;
+  const Shape s = plan(a->batch, a->vocab, a->dtype, ctas);
+  KParams P = make_params(a, s, workspace);
+  P.mode = 3;
+  P.topn = n;
+  P.top_ids = out_ids;
+  P.top_lp = out_logprobs;
+  return launch_sample(P, a->dtype, (cudaStream_t)stream);
 }
 
 int vinfer_sample_logprobs(const VinferSampleArgs* a, float* out_logprobs, void* workspace,

@@ -152,6 +152,26 @@ class B200Sampler:
                                                        self._stream()), "vinfer_sample_logprobs")
         return out
 
+    def top_logprobs(self, logits: torch.Tensor, params: RowParams, uniforms: torch.Tensor,
+                     history: TokenHistogram | None, n: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """The ``n`` most likely tokens of each row's final distribution and their
+        log-probabilities (``[B, n]`` int32 ids, float32 log-probabilities; -inf outside the
+        kept set, id -1 for an empty slot). Call right after ``sample_batch`` on the same
+        inputs: it prices tokens with the row results that call left."""
+        B, V = logits.shape
+        if not 1 <= n <= _lib.TOP_LOGPROBS_MAX or n >= V:
+            raise ValueError(f"n must be in [1, {_lib.TOP_LOGPROBS_MAX}] and below the vocabulary")
+        ids = torch.empty(B, n, dtype=torch.int32, device=self.device)
+        lp = torch.empty(B, n, dtype=torch.float32, device=self.device)
+        scratch = torch.empty(B, dtype=torch.int32, device=self.device)
+        a = self.args(logits, params, uniforms, history, scratch, None)
+        ws = self.workspace(B, V, a.dtype)
+        _lib.check(self.lib.vinfer_sample_top_logprobs(C.byref(a), n, ids.data_ptr(),
+                                                       lp.data_ptr(), ws.data_ptr(), ws.numel(),
+                                                       self._stream()),
+                   "vinfer_sample_top_logprobs")
+        return ids, lp
+
     # ---- batched decode with slotted histories ------------------------------------------------
     def append_tokens(self, slots: SlotHistogram, tokens: torch.Tensor) -> None:
         """Count ``tokens[s]`` once more in slot ``s`` (id order kept; a negative id is no
