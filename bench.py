@@ -848,10 +848,12 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["default", "config4", "topp"], default="default",
+    ap.add_argument("--workload", choices=["default", "config4", "config5", "topp"],
+                    default="default",
                     help="one GPU only: config4 times configuration 4 unsharded (the reference "
-                         "for the vocab-sharded runs); topp times configuration 3's logits with "
-                         "top-p only (the exact search); the default line is configuration 3")
+                         "for the vocab-sharded runs); config5 times configuration 5 (adversarial "
+                         "rows, mostly the exact search); topp times configuration 3's logits "
+                         "with top-p only (the exact search); the default line is configuration 3")
     args = ap.parse_args()
     rank, world, local = dist_env()
     if args.impl == "reference":
@@ -865,6 +867,19 @@ def main() -> None:
                          "torch.distributed.run with --nproc-per-node N")
     elif args.workload == "config4":
         line = bench_single_config4(args)
+    elif args.workload == "config5":
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        r = config_rows_per_s(5, dev, max(1, args.steps))
+        line = {"metric": METRIC, "value": r["rows_per_s"], "unit": "rows/s", "n_gpus": 1,
+                "steps": r["steps"], "warmup": 3, "ms_per_step": r["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic (seeded, configuration 5)",
+                "config": {"workload": "config5: batch 512 x vocab 151936 f32, flat / one +30 "
+                                       "token / 1000-way tie / N(0,1) rows, top-k U{1..1000}, "
+                                       "top-p U[0.1,1], temp U[0.1,2], 512-token histories",
+                           "batch": r["batch"], "vocab": r["vocab"]},
+                "method": {"l2": r["l2"], "timing": "sample_batch in CUDA graphs"}}
     else:
         line = bench_single(args)
     if line is not None and rank == 0:
