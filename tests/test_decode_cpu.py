@@ -55,3 +55,20 @@ def test_append_model():
     slots = [{3: 1}, {}, {1: 1, 2: 1}]
     full = append_model(slots, [3, -1, 4], cap=2)
     assert slots == [{3: 2}, {}, {1: 1, 2: 1}] and full
+
+
+def test_slots_from_csr_match_slots_from_token_lists():
+    rng = np.random.default_rng(2)
+    rows = [rng.integers(0, 500, rng.integers(0, 60)).tolist() for _ in range(7)]
+    a = SlotHistogram.from_token_lists(rows, 64, "cpu")
+    ptr, ids, cnt = [0], [], []
+    for toks in rows:
+        u, c = np.unique(np.asarray(toks, np.int64), return_counts=True)
+        ids.append(u.astype(np.int32))
+        cnt.append(c.astype(np.int32))
+        ptr.append(ptr[-1] + len(u))
+    b = SlotHistogram.from_csr(np.array(ptr), np.concatenate(ids), np.concatenate(cnt), 64, "cpu")
+    for name in ("ids", "counts", "lens", "row_ptr"):
+        assert np.array_equal(getattr(a, name).numpy(), getattr(b, name).numpy()), name
+    assert a.to_counts() == b.to_counts()
+    assert b.history.row_ptr.tolist() == [64 * s for s in range(8)]
