@@ -3315,8 +3315,9 @@ __device__ __forceinline__ int hist_pad_id(int cap, int p) {
 }
 
 // One CTA per slot: tokens[s] counted once more, or inserted in id order (entries from its place
-// on move up by one, chunk by chunk from the top, so no entry is overwritten before it is read).
-__global__ void __launch_bounds__(HIST_NT) k_hist_append(const int* tokens, int* ids, int* cnts,
+// on move up by one: read all, then written, when they fit the CTA's registers; otherwise chunk
+// by chunk from the top, so no entry is overwritten before it is read).
+__global__ void __launch_bounds__(HIST_NT, 2) k_hist_append(const int* tokens, int* ids, int* cnts,
                                                          int* lens, int cap, int* status) {
   // launched as a programmatic dependent of the sampler: its ids are final once the kernel
   // before this one has completed
@@ -3357,21 +3358,43 @@ __global__ void __launch_bounds__(HIST_NT) k_hist_append(const int* tokens, int*
     if (tid == 0 && status) atomicOr(reinterpret_cast<unsigned int*>(status), VINFER_ST_HIST_FULL);
     return;
   }
-  for (int hi = n; hi > pos; hi -= HIST_NT) {  // entries [lo, hi) move to [lo + 1, hi + 1)
-    const int lo = max(pos, hi - HIST_NT);
-    const int i = lo + tid;
-    int a = 0, c = 0;
-    if (i < hi) {
-      a = sid[i];
-      c = sc[i];
+  constexpr int PER = 8;  // entries a thread moves in the one-pass shift
+  if (n - pos <= PER * HIST_NT) {
+    // one pass: every entry of [pos, n) read into registers, then written one place up
+    int a[PER], c[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = pos + k * HIST_NT + tid;
+      a[k] = i < n ? sid[i] : 0;
+      c[k] = i < n ? sc[i] : 0;
     }
     __syncthreads();
-    if (i < hi) {
-      sid[i + 1] = a;
-      sc[i + 1] = c;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = pos + k * HIST_NT + tid;
+      if (i < n) {
+        sid[i + 1] = a[k];
+        sc[i + 1] = c[k];
+      }
     }
-    __syncthreads();
+  } else {
+    for (int hi = n; hi > pos; hi -= HIST_NT) {  // entries [lo, hi) move to [lo + 1, hi + 1)
+      const int lo = max(pos, hi - HIST_NT);
+      const int i = lo + tid;
+      int a = 0, c = 0;
+      if (i < hi) {
+        a = sid[i];
+        c = sc[i];
+      }
+      __syncthreads();
+      if (i < hi) {
+        sid[i + 1] = a;
+        sc[i + 1] = c;
+      }
+      __syncthreads();
+    }
   }
+  __syncthreads();
   if (tid == 0) {
     sid[pos] = t;
     sc[pos] = 1;
