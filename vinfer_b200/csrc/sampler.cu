@@ -3424,9 +3424,11 @@ struct Shape {
 // Segments per row and CTAs for a batch. A row is cut into at least enough segments of at most
 // SEG_BYTES. When the batch has fewer rows than the device has resident CTAs, each row is cut
 // into c = ctas / B runs of whole segments (nseg a multiple of c, segments of at least 2048
-// tokens), so every CTA streams one run; with as many rows as CTAs or more, the CTAs share the
-// row-major list of segments in equal contiguous ranges. One run per CTA pays the per-run
-// set-up once and leaves SM room for the finishing kernel to start early.
+// tokens), so every CTA streams one run. With as many rows as CTAs or more, each CTA takes r =
+// ceil(B / ctas) whole rows (the fewest CTAs that hold the batch; the CTAs share the row-major
+// list of segments in equal contiguous ranges, which are whole rows when r divides B): a row
+// then is one run, finished by its own CTA, instead of a run split over two CTAs whose second
+// must gather the first's record (measured on configuration 4: 198 against 216 us a batch).
 Shape plan(int64_t B, int64_t V, int dtype, int ctas) {
   const int es = dtype == VINFER_DTYPE_BF16 ? 2 : 4;
   const int A = 16 / es;
@@ -3443,7 +3445,12 @@ Shape plan(int64_t B, int64_t V, int dtype, int ctas) {
   Shape s;
   s.nseg = (int)nseg;
   s.seg_len = (int)len;
-  s.grid = (int)std::min<int64_t>(B * nseg, B < ctas ? B * c : ctas);
+  if (B < ctas) {
+    s.grid = (int)std::min<int64_t>(B * nseg, B * c);
+  } else {  // whole rows per CTA: r rows each, the fewest CTAs that hold the batch
+    const int64_t r = (B + ctas - 1) / ctas;
+    s.grid = (int)((B + r - 1) / r);
+  }
   return s;
 }
 
