@@ -267,12 +267,14 @@ def _hist_csr(rows):
     return np.array(ptr, np.int64), np.concatenate(ids_), np.concatenate(cnt)
 
 
-def test_large_batch_rows_split_across_ctas(backend):
-    # more rows than resident CTAs: CTAs take equal ranges of segments, so rows end up split
-    # across runs in every way (records merged by the finishing kernel)
-    w = make(2, batch=600, vocab=20_000)
+@pytest.mark.parametrize("batch", [600, 601])
+def test_large_batch_rows_split_across_ctas(backend, batch):
+    # more rows than resident CTAs: each CTA takes ceil(B / CTAs) rows' worth of the row-major
+    # segment list. 600 rows are whole rows per CTA; with 601 the CTAs' ranges cut rows, whose
+    # runs are finished by the CTA completing the row (records merged from two CTAs)
+    w = make(2, batch=batch, vocab=20_000)
     ids, probs = run_b200(backend, w, probs=False)
-    rows = list(range(0, 600, 7))
+    rows = list(range(0, batch, 7)) + [batch - 1]
     rep = compare(w, ids, None, rows=rows)
     assert not rep.failures, (str(rep), rep.failures[:5])
 
