@@ -183,6 +183,11 @@ int vinfer_sample_static(const VinferSampleArgs* args, void* stream);
  *  - vinfer_hist_reset: empty the n slots listed in slot_list (a request leaving its slot);
  *    entries outside [0, slots) are skipped.
  * Both are stream-ordered, one CTA per slot, and allocate nothing. cap <= VINFER_HIST_MAX_CAP.
+ *  - vinfer_sample_decode: vinfer_sample and vinfer_hist_append in one call. args' history
+ *    is the slotted arrays (row_ptr[s] = s * cap) and is updated in place with each row's
+ *    sampled id by the finishing kernel, after every read of it for this step; no out_probs.
+ *    A log-probability call (which prices tokens with the counts of the step) must instead
+ *    use vinfer_sample, vinfer_sample_logprobs, then vinfer_hist_append.
  */
 #define VINFER_HIST_PAD_ID 0x7FFFFFFF
 #define VINFER_HIST_MAX_CAP (1 << 20)
@@ -191,6 +196,8 @@ int vinfer_hist_append(const int32_t* tokens, int64_t slots, int32_t* hist_ids,
                        void* stream);
 int vinfer_hist_reset(const int32_t* slot_list, int64_t n, int64_t slots, int32_t* hist_ids,
                       int32_t* hist_counts, int32_t* hist_len, int32_t cap, void* stream);
+int vinfer_sample_decode(const VinferSampleArgs* args, int32_t* hist_len, int32_t cap,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

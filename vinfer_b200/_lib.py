@@ -39,6 +39,7 @@ EXPORTS = (
     "vinfer_sample_top_logprobs",
     "vinfer_hist_append",
     "vinfer_hist_reset",
+    "vinfer_sample_decode",
 )
 
 _ERRORS = {E_ARG: "invalid argument", E_LIMIT: "limit exceeded", E_CUDA: "CUDA error"}
@@ -114,6 +115,9 @@ def load() -> C.CDLL:
     lib.vinfer_hist_append.restype = C.c_int
     lib.vinfer_hist_append.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p,
                                        C.c_int32, C.c_void_p, C.c_void_p]
+    lib.vinfer_sample_decode.restype = C.c_int
+    lib.vinfer_sample_decode.argtypes = [C.POINTER(SampleArgs), C.c_void_p, C.c_int32, C.c_void_p,
+                                         C.c_size_t, C.c_void_p]
     lib.vinfer_hist_reset.restype = C.c_int
     lib.vinfer_hist_reset.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_int32, C.c_void_p]

@@ -128,6 +128,10 @@ struct KParams {
   int topn;          // mode 3: entries of each row's top list
   int* top_ids;      // mode 3: [B, topn] token ids (-1: none)
   float* top_lp;     // mode 3: [B, topn] log-probabilities
+  int* slot_ids;     // decode: the slotted histories (the same arrays as hids / hcnt), updated
+  int* slot_cnt;     //   in place by k_finish with each row's sampled id; null otherwise
+  int* hlen;         // decode: tokens held by each slot
+  int hcap;          // decode: entries of a slot
 };
 
 struct RowCfg {
@@ -2808,11 +2812,11 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
     // to complete before it exits itself.
     cbar();
     if (tid == 0) {
-      if (done) {
+      if (done && !P.slot_ids) {
         *reinterpret_cast<volatile int*>(P.counters + row) = CNT_DONE;
-      } else {
+      } else {  // records, or (decode) the row's id that k_finish counts into its slot
         __threadfence();
-        st_release(P.counters + row, CNT_READY);
+        st_release(P.counters + row, done ? CNT_DONE : CNT_READY);
       }
     }
     return;
@@ -2869,11 +2873,11 @@ __device__ __forceinline__ void run(const KParams& P, SSmem& X, int row, int seg
   }
   cbar();
   if (tid == 0) {
-    if (done) {
+    if (done && !P.slot_ids) {
       *reinterpret_cast<volatile int*>(P.counters + row) = CNT_DONE;
     } else {
       __threadfence();
-      st_release(P.counters + row, CNT_READY);
+      st_release(P.counters + row, done ? CNT_DONE : CNT_READY);
     }
   }
 }
@@ -2893,6 +2897,99 @@ __global__ void __launch_bounds__(NT, 2) k_stream(const __grid_constant__ KParam
     run<TIn>(P, X, row, seg_a, seg_b);
     cbar();
     sg = row * P.nseg + seg_b + 1;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// slotted histories (decode loop): one slot's in-place update
+// ---------------------------------------------------------------------------------------------
+constexpr int HIST_NT = 256;
+
+// padding id of position p of a slot with cap entries (ascending, above every vocabulary id)
+__device__ __forceinline__ int hist_pad_id(int cap, int p) {
+  return VINFER_HIST_PAD_ID - (cap - 1 - p);
+}
+
+// Counts token t once more in slot s, or inserts it in id order (entries from its place on move
+// up by one: read all, then written, when they fit the CTA's registers; otherwise chunk by chunk
+// from the top, so no entry is overwritten before it is read). The whole CTA (HIST_NT threads).
+__device__ __forceinline__ void slot_append(int* ids, int* cnts, int* lens, int cap, int s, int t,
+                                            int* status) {
+  const int tid = threadIdx.x;
+  int* sid = ids + (int64_t)s * cap;
+  int* sc = cnts + (int64_t)s * cap;
+  const int n = min(max(lens[s], 0), cap);
+  __shared__ int pos_s, found_s;
+  if (tid < 32) {
+    // the first entry whose id is >= t: a warp-wide search, 32 probes per round (each round
+    // narrows [lo, hi] to a 33rd); the predicate sid[q] < t is monotone in q
+    int lo = 0, hi = n;
+    while (hi - lo > 32) {
+      const int step = (hi - lo + 32) / 33;
+      const int q = min(lo + (tid + 1) * step, hi) - 1;
+      const int k = __popc(__ballot_sync(FULLMASK, sid[q] < t));
+      const int nlo = min(lo + k * step, hi);
+      if (k < 32) hi = min(lo + (k + 1) * step, hi);
+      lo = nlo;
+    }
+    const int q = lo + tid;
+    const int pos = lo + __popc(__ballot_sync(FULLMASK, q < hi && sid[q] < t));
+    if (tid == 0) {
+      pos_s = pos;
+      found_s = pos < n && sid[pos] == t;
+    }
+  }
+  __syncthreads();
+  const int pos = pos_s;
+  if (found_s) {
+    if (tid == 0) sc[pos] += 1;
+    return;
+  }
+  if (n >= cap) {
+    if (tid == 0 && status) atomicOr(reinterpret_cast<unsigned int*>(status), VINFER_ST_HIST_FULL);
+    return;
+  }
+  constexpr int PER = 8;  // entries a thread moves in the one-pass shift
+  if (n - pos <= PER * HIST_NT) {
+    // one pass: every entry of [pos, n) read into registers, then written one place up
+    int a[PER], c[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = pos + k * HIST_NT + tid;
+      a[k] = i < n ? sid[i] : 0;
+      c[k] = i < n ? sc[i] : 0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = pos + k * HIST_NT + tid;
+      if (i < n) {
+        sid[i + 1] = a[k];
+        sc[i + 1] = c[k];
+      }
+    }
+  } else {
+    for (int hi = n; hi > pos; hi -= HIST_NT) {  // entries [lo, hi) move to [lo + 1, hi + 1)
+      const int lo = max(pos, hi - HIST_NT);
+      const int i = lo + tid;
+      int a = 0, c = 0;
+      if (i < hi) {
+        a = sid[i];
+        c = sc[i];
+      }
+      __syncthreads();
+      if (i < hi) {
+        sid[i + 1] = a;
+        sc[i + 1] = c;
+      }
+      __syncthreads();
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    sid[pos] = t;
+    sc[pos] = 1;
+    lens[s] = n + 1;
   }
 }
 
@@ -3220,6 +3317,16 @@ __global__ void __launch_bounds__(NT, 3) k_finish(const __grid_constant__ KParam
   } else {
     finish_ready<TIn>(P, S);
   }
+  if (P.slot_ids) {
+    // decode: the row's id, final now (written by this CTA, or by the streaming kernel before
+    // its release of the mark this CTA acquired), counted into the row's slot; every read of
+    // the slot's history for this step is over
+    cbar();
+    if (tid == 0) S.sc[SC_J] = __ldcg(P.out_ids + row);
+    cbar();
+    const int t = S.sc[SC_J];
+    if (t >= 0) slot_append(P.slot_ids, P.slot_cnt, P.hlen, P.hcap, row, t, P.status);
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
@@ -3307,99 +3414,15 @@ __global__ void __launch_bounds__(128) k_logprobs(const __grid_constant__ KParam
 // ---------------------------------------------------------------------------------------------
 // slotted histories: in-place count updates between decode steps
 // ---------------------------------------------------------------------------------------------
-constexpr int HIST_NT = 256;
-
-// padding id of position p of a slot with cap entries (ascending, above every vocabulary id)
-__device__ __forceinline__ int hist_pad_id(int cap, int p) {
-  return VINFER_HIST_PAD_ID - (cap - 1 - p);
-}
-
-// One CTA per slot: tokens[s] counted once more, or inserted in id order (entries from its place
-// on move up by one: read all, then written, when they fit the CTA's registers; otherwise chunk
-// by chunk from the top, so no entry is overwritten before it is read).
+// One CTA per slot: tokens[s] counted once more in slot s (slot_append).
 __global__ void __launch_bounds__(HIST_NT, 2) k_hist_append(const int* tokens, int* ids, int* cnts,
                                                          int* lens, int cap, int* status) {
   // launched as a programmatic dependent of the sampler: its ids are final once the kernel
   // before this one has completed
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int s = blockIdx.x, tid = threadIdx.x;
-  const int t = tokens[s];
+  const int t = tokens[blockIdx.x];
   if (t < 0) return;  // no token this step (an invalid row's id is -1)
-  int* sid = ids + (int64_t)s * cap;
-  int* sc = cnts + (int64_t)s * cap;
-  const int n = min(max(lens[s], 0), cap);
-  __shared__ int pos_s, found_s;
-  if (tid < 32) {
-    // the first entry whose id is >= t: a warp-wide search, 32 probes per round (each round
-    // narrows [lo, hi] to a 33rd); the predicate sid[q] < t is monotone in q
-    int lo = 0, hi = n;
-    while (hi - lo > 32) {
-      const int step = (hi - lo + 32) / 33;
-      const int q = min(lo + (tid + 1) * step, hi) - 1;
-      const int k = __popc(__ballot_sync(FULLMASK, sid[q] < t));
-      const int nlo = min(lo + k * step, hi);
-      if (k < 32) hi = min(lo + (k + 1) * step, hi);
-      lo = nlo;
-    }
-    const int q = lo + tid;
-    const int pos = lo + __popc(__ballot_sync(FULLMASK, q < hi && sid[q] < t));
-    if (tid == 0) {
-      pos_s = pos;
-      found_s = pos < n && sid[pos] == t;
-    }
-  }
-  __syncthreads();
-  const int pos = pos_s;
-  if (found_s) {
-    if (tid == 0) sc[pos] += 1;
-    return;
-  }
-  if (n >= cap) {
-    if (tid == 0 && status) atomicOr(reinterpret_cast<unsigned int*>(status), VINFER_ST_HIST_FULL);
-    return;
-  }
-  constexpr int PER = 8;  // entries a thread moves in the one-pass shift
-  if (n - pos <= PER * HIST_NT) {
-    // one pass: every entry of [pos, n) read into registers, then written one place up
-    int a[PER], c[PER];
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      const int i = pos + k * HIST_NT + tid;
-      a[k] = i < n ? sid[i] : 0;
-      c[k] = i < n ? sc[i] : 0;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      const int i = pos + k * HIST_NT + tid;
-      if (i < n) {
-        sid[i + 1] = a[k];
-        sc[i + 1] = c[k];
-      }
-    }
-  } else {
-    for (int hi = n; hi > pos; hi -= HIST_NT) {  // entries [lo, hi) move to [lo + 1, hi + 1)
-      const int lo = max(pos, hi - HIST_NT);
-      const int i = lo + tid;
-      int a = 0, c = 0;
-      if (i < hi) {
-        a = sid[i];
-        c = sc[i];
-      }
-      __syncthreads();
-      if (i < hi) {
-        sid[i + 1] = a;
-        sc[i + 1] = c;
-      }
-      __syncthreads();
-    }
-  }
-  __syncthreads();
-  if (tid == 0) {
-    sid[pos] = t;
-    sc[pos] = 1;
-    lens[s] = n + 1;
-  }
+  slot_append(ids, cnts, lens, cap, blockIdx.x, t, status);
 }
 
 // One CTA per listed slot: every entry back to padding, the length to zero.
@@ -3725,6 +3748,27 @@ int vinfer_sample_top_logprobs(const VinferSampleArgs* a, int32_t n, int32_t* ou
   P.topn = n;
   P.top_ids = out_ids;
   P.top_lp = out_logprobs;
+  return launch_sample(P, a->dtype, (cudaStream_t)stream);
+}
+
+int vinfer_sample_decode(const VinferSampleArgs* a, int32_t* hist_len, int32_t cap,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  NvtxRange nvtx_range("vinfer_sample_decode");
+  int rc = check_args(a);
+  if (rc != VINFER_OK) return rc;
+  if (a->vocab_offset != 0 || a->vocab_total != a->vocab) return VINFER_E_ARG;
+  if (!workspace || !hist_len || !a->hist_row_ptr || a->out_probs || cap < 1) return VINFER_E_ARG;
+  if (cap > VINFER_HIST_MAX_CAP) return VINFER_E_LIMIT;
+  if (workspace_bytes < ws_layout(a->batch, a->vocab, a->dtype).total) return VINFER_E_LIMIT;
+  int ctas = 0;
+  if (sample_ctas(a->dtype, &ctas) != VINFER_OK) return VINFER_E_CUDA;
+  const Shape s = plan(a->batch, a->vocab, a->dtype, ctas);
+  KParams P = make_params(a, s, workspace);
+  P.mode = 0;
+  P.slot_ids = const_cast<int*>(a->hist_ids);  // the caller's slotted arrays, updated in place
+  P.slot_cnt = const_cast<int*>(a->hist_counts);
+  P.hlen = hist_len;
+  P.hcap = cap;
   return launch_sample(P, a->dtype, (cudaStream_t)stream);
 }
 

@@ -198,10 +198,20 @@ class B200Sampler:
 
     def decode_step(self, logits: torch.Tensor, params: RowParams, uniforms: torch.Tensor,
                     slots: SlotHistogram, out: torch.Tensor | None = None) -> torch.Tensor:
-        """One decode step of every slot: sample with the slots' histories (penalties), then
-        count the sampled ids into them. Nothing leaves the device; the ids are in ``out``."""
-        out = self.sample_batch(logits, params, uniforms, slots.history, out=out)
-        self.append_tokens(slots, out)
+        """One decode step of every slot: sample with the slots' histories (penalties) and count
+        the sampled ids into them, in one call (``vinfer_sample_decode``: the finishing kernel
+        updates each row's slot once the row is decided). Nothing leaves the device; the ids
+        are in ``out``."""
+        B, V = logits.shape
+        if slots.slots != B:
+            raise ValueError(f"{slots.slots} slots for {B} rows")
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=self.device)
+        a = self.args(logits, params, uniforms, slots.history, out, None)
+        ws = self.workspace(B, V, a.dtype)
+        _lib.check(self.lib.vinfer_sample_decode(C.byref(a), slots.lens.data_ptr(), slots.cap,
+                                                 ws.data_ptr(), ws.numel(), self._stream()),
+                   "vinfer_sample_decode")
         return out
 
     def sample(self, logits: torch.Tensor, params: SamplingParams, seed: int,
